@@ -1,0 +1,107 @@
+/*
+ * npu_b200.h - C ABI of libnpub200, the B200 (sm_100a) backend of the npu-ai offload hot path.
+ *
+ * The reference (Tobynau/npu-ai) drives an AMD XDNA1 NPU from Python: `NpuGemm` in npu/xdna1_gemm.py builds
+ * buffers and calls `NpuProgram.submit_gemm` / `submit_attn` (npu/xdna1_program.py:451-473), which hand three
+ * buffer objects and 13 int32 parameters to one XRT kernel command (xdna1_program.py:441-446). This header is
+ * the B200 equivalent of that dispatch boundary: plain device pointers, sizes and element strides, a CUDA stream
+ * passed as `void*` (a cudaStream_t; NULL = the legacy default stream), no torch types. Everything launches
+ * asynchronously on the given stream; nothing here synchronises except npub200_status_read.
+ *
+ * Conventions
+ *   - bf16 tensors are `uint16_t` bit patterns (__nv_bfloat16 / torch.bfloat16); dtype codes below.
+ *   - Strides are in elements. The innermost dimension is always contiguous.
+ *   - Return value: 0 on success, a negative NPUB200_E* code on failure; npub200_last_error() then holds a
+ *     message for the calling thread. There is no CPU fallback: a request no kernel variant takes fails.
+ *   - Kernels never trap. A bounded wait that expires inside a kernel sets bits in the device's status word;
+ *     npub200_status_read() reports them (the reference's `NpuProgram.wait` raising RuntimeError,
+ *     xdna1_program.py:475-479).
+ */
+#ifndef NPU_B200_H_
+#define NPU_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NPUB200_OK 0
+#define NPUB200_EINVAL (-1)      /* invalid shape, stride, alignment or dtype */
+#define NPUB200_ECUDA (-2)       /* a CUDA runtime/driver call failed */
+#define NPUB200_EUNSUPPORTED (-3) /* legal request without a kernel variant in this build */
+#define NPUB200_EDEVICE (-4)     /* a kernel reported a failure (see npub200_status_read) */
+
+#define NPUB200_DTYPE_BF16 0
+#define NPUB200_DTYPE_F32 1
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int npub200_version(void);
+
+/* Message of the last failing call made by this thread ("" if none). */
+const char* npub200_last_error(void);
+
+/* Number of SMs of the current device (initialises the library's per-device state). */
+int npub200_device_sms(int* sms_out);
+
+/* ----------------------------------------------------------------------------------------------------------
+ * Resident weights. Replaces NpuGemm.upload_weight / NpuWeight (npu/xdna1_gemm.py:311-321, :89-99): the weight
+ * stays in HBM in nn.Linear's own [N, K] layout (no transpose, no padding copy) and the handle caches the TMA
+ * descriptors built for it. `w` must stay allocated until npub200_weight_release. K % 8 == 0 and ldw % 8 == 0
+ * with a 16-byte aligned base (TMA addressing); callers pad other weights once at upload.
+ * ---------------------------------------------------------------------------------------------------------- */
+int npub200_weight_register(const void* w, int64_t n, int64_t k, int64_t ldw, int64_t* handle_out);
+int npub200_weight_release(int64_t handle);
+
+/* ----------------------------------------------------------------------------------------------------------
+ * GEMM: out[M, N] = x[M, K] . W[N, K]^T (+ bias[N]); bf16 operands, f32 accumulation, bias added in f32,
+ * out f32 or bf16. Replaces NpuGemm.matmul_t (npu/xdna1_gemm.py:349-422) and the GEMM mode of the unified NPU
+ * program (npu/xdna1_program.py:451-454, npu/kernels/xdna1_attn.cc:480-574). Any M, N, K >= 1: ragged tails are
+ * handled in the kernel. x rows need a 16-byte aligned base and ldx % 8 == 0 (TMA); otherwise x is first
+ * repacked into `workspace`, which must then hold npub200_gemm_workspace_size() bytes (NULL/0 is fine when that
+ * size is 0). `variant` 0 picks the tile automatically, or forces an N tile in {64, 80, 128, 160, 256}.
+ * ---------------------------------------------------------------------------------------------------------- */
+int npub200_gemm_workspace_size(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw,
+                                int64_t n, size_t* bytes_out);
+int npub200_gemm(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                 const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace,
+                 size_t workspace_bytes, int variant, void* stream);
+/* Same with a registered weight (the resident-weight path the runner uses). */
+int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t weight, const void* bias,
+                   int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace, size_t workspace_bytes,
+                   int variant, void* stream);
+
+/* ----------------------------------------------------------------------------------------------------------
+ * Fused attention: out = softmax(Q K^T * scale) V for every (batch, head) pair in ONE launch; bf16 q/k/v,
+ * f32 softmax statistics and accumulation, out bf16 or f32. Replaces NpuGemm.attention / _attention_fused
+ * (npu/xdna1_gemm.py:499-752), NpuProgram.submit_attn (npu/xdna1_program.py:461-473) and the AIE flash kernel
+ * (npu/kernels/xdna1_attn.cc:342-445). Element (b, s, h, e) of a tensor lives at b*sb + s*ss + h*sh + e, so both
+ * the model's (B, S, H*D) layout and the head-major (B, H, S, D) layout (`skip_reshape`) are strided views.
+ * Strides must be multiples of 8 elements and bases 16-byte aligned (TMA). Head dims 40, 80, 160 (any multiple
+ * of 8 up to 256 is accepted); any Sq, Skv >= 1 (key tails are masked in the kernel, no padding).
+ * ---------------------------------------------------------------------------------------------------------- */
+int npub200_attention(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, const void* k, int64_t k_sb,
+                      int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                      void* out, int64_t o_sb, int64_t o_ss, int64_t o_sh, int out_dtype, int64_t batch,
+                      int64_t heads, int64_t sq, int64_t skv, int64_t head_dim, float scale, int variant,
+                      void* stream);
+
+/* ----------------------------------------------------------------------------------------------------------
+ * Device status word (failure detection; the reference's RuntimeError from NpuProgram.wait,
+ * npu/xdna1_program.py:475-479). Synchronises `stream`, returns the OR of the status bits kernels on the current
+ * device reported since the last clear (0 = healthy), and clears them when `clear` is non-zero.
+ * ---------------------------------------------------------------------------------------------------------- */
+int npub200_status_read(void* stream, uint32_t* bits_out, int clear);
+
+/* Test hooks (failure detection without a GPU fault): per-wait deadline in ns (0 restores the default), and
+ * debug flags applied to the next launches (bit 0: the MMA role waits on a barrier nothing signals, so the
+ * bounded wait expires and the kernel takes its abort path). */
+int npub200_set_wait_timeout_ns(uint64_t ns);
+int npub200_set_debug_flags(uint32_t flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NPU_B200_H_ */

@@ -1,0 +1,357 @@
+// capi.cu - the extern "C" entry points of libnpub200 (declared in include/npu_b200.h) and the host plumbing
+// behind them: argument checks, per-device state (SM count, status word), TMA descriptor encoding, and the
+// resident-weight registry.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "../../include/npu_b200.h"
+#include "internal.h"
+
+namespace npub200 {
+
+// One status word per device; kernels OR StatusBits into it. Read and cleared by npub200_status_read.
+__device__ uint32_t g_status_word;
+
+namespace {
+
+thread_local char g_last_error[1024] = {0};
+std::mutex g_dev_mutex;
+DeviceInfo g_devices[64];
+std::atomic<uint64_t> g_timeout_ns{0};
+std::atomic<uint32_t> g_debug_flags{0};
+constexpr uint64_t kDefaultTimeoutNs = 4000000000ull;  // 4 s per wait: far above any legitimate stall
+
+struct WeightEntry {
+  const void* w;
+  int64_t n, k, ldw;
+  int device;
+  std::unordered_map<int, CUtensorMap> maps;  // per N tile
+};
+std::mutex g_w_mutex;
+std::unordered_map<int64_t, WeightEntry> g_weights;
+int64_t g_next_handle = 1;
+
+}  // namespace
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return kOk;
+  return fail(kErrCuda, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+uint64_t wait_timeout_ns() {
+  const uint64_t t = g_timeout_ns.load();
+  return t ? t : kDefaultTimeoutNs;
+}
+
+int current_device_info(const DeviceInfo** out) {
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64) return fail(kErrInvalid, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  DeviceInfo& d = g_devices[dev];
+  if (d.device < 0) {
+    cudaDeviceProp prop;
+    if (int rc = check_cuda(cudaGetDeviceProperties(&prop, dev), "cudaGetDeviceProperties")) return rc;
+    if (prop.major != 10)
+      return fail(kErrUnsupported, "device %d (%s, sm_%d%d) is not a B200-class sm_100 GPU", dev, prop.name,
+                  prop.major, prop.minor);
+    void* p = nullptr;
+    if (int rc = check_cuda(cudaGetSymbolAddress(&p, g_status_word), "cudaGetSymbolAddress(status)")) return rc;
+    d.sms = prop.multiProcessorCount;
+    d.smem_optin = int(prop.sharedMemPerBlockOptin);
+    d.cc_major = prop.major;
+    d.cc_minor = prop.minor;
+    d.status = static_cast<uint32_t*>(p);
+    d.device = dev;
+  }
+  *out = &d;
+  return kOk;
+}
+
+int encode_tiled_fn(EncodeTiledFn* out) {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  static int rc_once = kOk;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || p == nullptr) {
+      rc_once = kErrCuda;
+    } else {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  if (fn == nullptr) return fail(kErrCuda, "cuTensorMapEncodeTiled is unavailable from the CUDA driver");
+  *out = fn;
+  return rc_once;
+}
+
+}  // namespace npub200
+
+using namespace npub200;
+
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// TMA needs a 16-byte aligned base, a row stride that is a multiple of 16 bytes and >= the row length.
+bool tma_rows_ok(const void* p, int64_t ld, int64_t cols) { return aligned16(p) && ld % 8 == 0 && ld >= cols; }
+
+int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+
+size_t gemm_ws_bytes(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n) {
+  const int64_t kp = round_up(k, 8);
+  size_t bytes = 0;
+  const bool pad_k = (k % 8) != 0;
+  if (pad_k || !tma_rows_ok(x, ldx, k)) bytes += size_t(round_up(m * kp * 2, 256));
+  if (w != nullptr && (pad_k || !tma_rows_ok(w, ldw, k))) bytes += size_t(round_up(n * kp * 2, 256));
+  return bytes;
+}
+
+int check_gemm_common(int64_t m, int64_t k, int64_t n, int bias_dtype, const void* out, int64_t ldo,
+                      int out_dtype) {
+  if (m <= 0 || k <= 0 || n <= 0)
+    return fail(kErrInvalid, "GEMM sizes must be positive (M=%lld K=%lld N=%lld)", (long long)m, (long long)k,
+                (long long)n);
+  if (out == nullptr) return fail(kErrInvalid, "GEMM output pointer is null");
+  if (ldo < n) return fail(kErrInvalid, "output row stride %lld < N=%lld", (long long)ldo, (long long)n);
+  if (out_dtype != NPUB200_DTYPE_BF16 && out_dtype != NPUB200_DTYPE_F32)
+    return fail(kErrInvalid, "unknown output dtype code %d", out_dtype);
+  if (bias_dtype != NPUB200_DTYPE_BF16 && bias_dtype != NPUB200_DTYPE_F32)
+    return fail(kErrInvalid, "unknown bias dtype code %d", bias_dtype);
+  return kOk;
+}
+
+int gemm_common(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                const CUtensorMap* w_map, const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
+                void* workspace, size_t workspace_bytes, int variant, void* stream) {
+  if (x == nullptr || w == nullptr) return fail(kErrInvalid, "GEMM operand pointer is null");
+  if (ldx < k) return fail(kErrInvalid, "x row stride %lld < K=%lld", (long long)ldx, (long long)k);
+  if (ldw < k) return fail(kErrInvalid, "W row stride %lld < K=%lld", (long long)ldw, (long long)k);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GemmProblem p;
+  memset(&p, 0, sizeof(p));
+  p.x = x;
+  p.ldx = ldx;
+  p.w = w;
+  p.ldw = ldw;
+  p.bias = bias;
+  p.bias_f32 = bias_dtype == NPUB200_DTYPE_F32;
+  p.out = out;
+  p.ldo = ldo;
+  p.out_f32 = out_dtype == NPUB200_DTYPE_F32;
+  p.M = m;
+  p.N = n;
+  p.K = k;
+  p.variant = variant;
+  p.w_map_cache = w_map;
+  p.debug = g_debug_flags.load();
+
+  const bool pad_k = (k % 8) != 0;
+  const bool x_ok = !pad_k && tma_rows_ok(x, ldx, k);
+  const bool w_ok = !pad_k && tma_rows_ok(w, ldw, k);
+  if (!x_ok || !w_ok) {
+    // Workspace path: dense copies with K padded to a multiple of 8 (zero columns add nothing to the dot products).
+    const size_t need = gemm_ws_bytes(x, ldx, m, k, w, ldw, n);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(kErrInvalid, "this GEMM needs a %zu-byte workspace (operands are not TMA-addressable), got %zu",
+                  need, workspace_bytes);
+    if (!aligned16(workspace)) return fail(kErrInvalid, "workspace must be 16-byte aligned");
+    const int64_t kp = round_up(k, 8);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    if (!x_ok) {
+      if (int rc = repack_rows_bf16(x, ldx, m, k, ws, kp, st)) return rc;
+      p.x = ws;
+      p.ldx = kp;
+      ws += round_up(m * kp * 2, 256);
+    }
+    if (!w_ok) {
+      if (int rc = repack_rows_bf16(w, ldw, n, k, ws, kp, st)) return rc;
+      p.w = ws;
+      p.ldw = kp;
+      p.w_map_cache = nullptr;
+    }
+    if (pad_k) {
+      p.K = kp;
+      if (x_ok) return fail(kErrInvalid, "internal: K padding requires a repacked x");
+    }
+  }
+  return gemm_launch(p, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int npub200_version(void) { return 100; }
+
+const char* npub200_last_error(void) { return g_last_error; }
+
+int npub200_device_sms(int* sms_out) {
+  const DeviceInfo* d = nullptr;
+  if (int rc = current_device_info(&d)) return rc;
+  if (sms_out) *sms_out = d->sms;
+  return kOk;
+}
+
+int npub200_weight_register(const void* w, int64_t n, int64_t k, int64_t ldw, int64_t* handle_out) {
+  if (w == nullptr || handle_out == nullptr) return fail(kErrInvalid, "null weight or handle pointer");
+  if (n <= 0 || k <= 0) return fail(kErrInvalid, "weight sizes must be positive (N=%lld K=%lld)", (long long)n,
+                                    (long long)k);
+  if (k % 8 != 0 || !tma_rows_ok(w, ldw, k))
+    return fail(kErrInvalid,
+                "resident weights need K %% 8 == 0, ldw %% 8 == 0 and a 16-byte aligned base (got K=%lld ldw=%lld)",
+                (long long)k, (long long)ldw);
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  std::lock_guard<std::mutex> lock(g_w_mutex);
+  const int64_t h = g_next_handle++;
+  WeightEntry e;
+  e.w = w;
+  e.n = n;
+  e.k = k;
+  e.ldw = ldw;
+  e.device = dev;
+  g_weights.emplace(h, std::move(e));
+  *handle_out = h;
+  return kOk;
+}
+
+int npub200_weight_release(int64_t handle) {
+  std::lock_guard<std::mutex> lock(g_w_mutex);
+  if (g_weights.erase(handle) == 0) return fail(kErrInvalid, "unknown weight handle %lld", (long long)handle);
+  return kOk;
+}
+
+int npub200_gemm_workspace_size(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw,
+                                int64_t n, size_t* bytes_out) {
+  if (bytes_out == nullptr) return fail(kErrInvalid, "null output pointer");
+  *bytes_out = gemm_ws_bytes(x, ldx, m, k, w, ldw, n);
+  return kOk;
+}
+
+int npub200_gemm(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                 const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace,
+                 size_t workspace_bytes, int variant, void* stream) {
+  if (int rc = check_gemm_common(m, k, n, bias_dtype, out, ldo, out_dtype)) return rc;
+  return gemm_common(x, ldx, m, k, w, ldw, n, nullptr, bias, bias_dtype, out, ldo, out_dtype, workspace,
+                     workspace_bytes, variant, stream);
+}
+
+int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t weight, const void* bias,
+                   int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace, size_t workspace_bytes,
+                   int variant, void* stream) {
+  const void* w = nullptr;
+  int64_t n = 0, ldw = 0;
+  CUtensorMap map;
+  const CUtensorMap* map_ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_w_mutex);
+    auto it = g_weights.find(weight);
+    if (it == g_weights.end()) return fail(kErrInvalid, "unknown weight handle %lld", (long long)weight);
+    WeightEntry& e = it->second;
+    if (e.k != k) return fail(kErrInvalid, "K mismatch: x has %lld, weight has %lld", (long long)k, (long long)e.k);
+    w = e.w;
+    n = e.n;
+    ldw = e.ldw;
+    if (int rc = check_gemm_common(m, k, n, bias_dtype, out, ldo, out_dtype)) return rc;
+    const DeviceInfo* d = nullptr;
+    if (int rc = current_device_info(&d)) return rc;
+    if (d->device != e.device) return fail(kErrInvalid, "weight was registered on device %d, current is %d",
+                                           e.device, d->device);
+    const int bn = variant ? variant : gemm_pick_bn(m, n, k, d->sms);
+    auto mit = e.maps.find(bn);
+    if (mit == e.maps.end()) {
+      CUtensorMap fresh;
+      if (int rc = gemm_encode_b_map(e.w, e.ldw, e.n, e.k, bn, &fresh)) return rc;
+      mit = e.maps.emplace(bn, fresh).first;
+    }
+    map = mit->second;
+    map_ptr = &map;
+    variant = bn;
+  }
+  return gemm_common(x, ldx, m, k, w, ldw, n, map_ptr, bias, bias_dtype, out, ldo, out_dtype, workspace,
+                     workspace_bytes, variant, stream);
+}
+
+int npub200_attention(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, const void* k, int64_t k_sb,
+                      int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                      void* out, int64_t o_sb, int64_t o_ss, int64_t o_sh, int out_dtype, int64_t batch,
+                      int64_t heads, int64_t sq, int64_t skv, int64_t head_dim, float scale, int variant,
+                      void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+    return fail(kErrInvalid, "attention tensor pointer is null");
+  if (batch <= 0 || heads <= 0 || sq <= 0 || skv <= 0 || head_dim <= 0)
+    return fail(kErrInvalid, "attention sizes must be positive (B=%lld H=%lld Sq=%lld Skv=%lld D=%lld)",
+                (long long)batch, (long long)heads, (long long)sq, (long long)skv, (long long)head_dim);
+  if (out_dtype != NPUB200_DTYPE_BF16 && out_dtype != NPUB200_DTYPE_F32)
+    return fail(kErrInvalid, "unknown output dtype code %d", out_dtype);
+  AttnProblem p;
+  memset(&p, 0, sizeof(p));
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.o = out;
+  p.q_sb = q_sb;
+  p.q_ss = q_ss;
+  p.q_sh = q_sh;
+  p.k_sb = k_sb;
+  p.k_ss = k_ss;
+  p.k_sh = k_sh;
+  p.v_sb = v_sb;
+  p.v_ss = v_ss;
+  p.v_sh = v_sh;
+  p.o_sb = o_sb;
+  p.o_ss = o_ss;
+  p.o_sh = o_sh;
+  p.B = batch;
+  p.H = heads;
+  p.Sq = sq;
+  p.Skv = skv;
+  p.D = head_dim;
+  p.scale = scale;
+  p.out_f32 = out_dtype == NPUB200_DTYPE_F32;
+  p.variant = variant;
+  p.debug = g_debug_flags.load();
+  return attention_launch(p, static_cast<cudaStream_t>(stream));
+}
+
+int npub200_status_read(void* stream, uint32_t* bits_out, int clear) {
+  const DeviceInfo* d = nullptr;
+  if (int rc = current_device_info(&d)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = check_cuda(cudaStreamSynchronize(st), "cudaStreamSynchronize")) return rc;
+  uint32_t bits = 0;
+  if (int rc = check_cuda(cudaMemcpyFromSymbol(&bits, g_status_word, sizeof(bits)), "read status word")) return rc;
+  if (clear && bits) {
+    const uint32_t zero = 0;
+    if (int rc = check_cuda(cudaMemcpyToSymbol(g_status_word, &zero, sizeof(zero)), "clear status word")) return rc;
+  }
+  if (bits_out) *bits_out = bits;
+  return kOk;
+}
+
+int npub200_set_wait_timeout_ns(uint64_t ns) {
+  g_timeout_ns.store(ns);
+  return kOk;
+}
+
+int npub200_set_debug_flags(uint32_t flags) {
+  g_debug_flags.store(flags);
+  return kOk;
+}
+
+}  // extern "C"

@@ -1,0 +1,86 @@
+// internal.h - host-side plumbing shared by the translation units of libnpub200 (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "sm100_ptx.cuh"
+
+namespace npub200 {
+
+// Error codes returned by the C entry points (mirrored in include/npu_b200.h).
+constexpr int kOk = 0;
+constexpr int kErrInvalid = -1;      // bad shape / stride / alignment / dtype: the caller's mistake
+constexpr int kErrCuda = -2;         // a CUDA runtime or driver call failed
+constexpr int kErrUnsupported = -3;  // a legal request this build has no kernel variant for
+constexpr int kErrDevice = -4;       // a kernel reported a failure through its status word
+
+// Records the message of the last failing call on this thread and returns `code`.
+int fail(int code, const char* fmt, ...);
+int check_cuda(cudaError_t e, const char* what);
+
+struct DeviceInfo {
+  int device = -1;
+  int sms = 0;
+  int smem_optin = 0;
+  int cc_major = 0, cc_minor = 0;
+  uint32_t* status = nullptr;  // device address of this device's status word
+};
+// Cached properties of the current device (initialised on first use per device).
+int current_device_info(const DeviceInfo** out);
+
+// Per-wait deadline handed to kernels (nanoseconds); tests shorten it through the C ABI.
+uint64_t wait_timeout_ns();
+
+// cuTensorMapEncodeTiled, resolved through the runtime's driver entry point (no link-time libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+int encode_tiled_fn(EncodeTiledFn* out);
+
+// ---- GEMM --------------------------------------------------------------------------------------------------------
+struct GemmProblem {
+  const void* x;  // [M, K] bf16, row stride ldx elements
+  int64_t ldx;
+  const void* w;  // [N, K] bf16 (nn.Linear layout), row stride ldw elements
+  int64_t ldw;
+  const void* bias;  // [N] or null
+  int bias_f32;      // 1: bias is f32, 0: bf16
+  void* out;         // [M, N], row stride ldo elements
+  int64_t ldo;
+  int out_f32;       // 1: f32 output, 0: bf16
+  int64_t M, N, K;
+  int variant;       // 0 = automatic, else a forced N tile (64, 80, 128, 160, 256)
+  const CUtensorMap* w_map_cache;  // optional cached B tensor map (matching the chosen tile), may be null
+  uint32_t debug;
+};
+// Chooses the N tile for a problem (what `variant == 0` resolves to).
+int gemm_pick_bn(int64_t M, int64_t N, int64_t K, int sms);
+int gemm_encode_b_map(const void* w, int64_t ldw, int64_t N, int64_t K, int bn, CUtensorMap* out);
+int gemm_launch(const GemmProblem& p, cudaStream_t stream);
+// bf16 copy of a row-strided matrix into a dense [rows, cols_pad] buffer, zero-filling the pad columns.
+int repack_rows_bf16(const void* src, int64_t ld_src, int64_t rows, int64_t cols, void* dst, int64_t cols_pad,
+                     cudaStream_t stream);
+
+// ---- attention ---------------------------------------------------------------------------------------------------
+struct AttnProblem {
+  const void* q;  // bf16, element (b, s, h, e) at b*sb + s*ss + h*sh + e
+  const void* k;
+  const void* v;
+  void* o;
+  int64_t q_sb, q_ss, q_sh;
+  int64_t k_sb, k_ss, k_sh;
+  int64_t v_sb, v_ss, v_sh;
+  int64_t o_sb, o_ss, o_sh;
+  int64_t B, H, Sq, Skv, D;
+  float scale;
+  int out_f32;
+  int variant;
+  uint32_t debug;
+};
+int attention_launch(const AttnProblem& p, cudaStream_t stream);
+
+}  // namespace npub200

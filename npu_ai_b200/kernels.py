@@ -1,0 +1,172 @@
+"""Tensor-level calls into libnpub200: torch CUDA tensors in, pointers/strides through the C ABI, torch out.
+
+torch provides device memory and the current stream; the arithmetic runs in the sm_100a kernels of the
+library. Nothing here computes on the CPU, and there is no fallback when a kernel refuses a request.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_DT = {torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (got {t.device})")
+
+
+def device_sms(device: torch.device | int | None = None) -> int:
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        n = ctypes.c_int(0)
+        _lib.call("npub200_device_sms", ctypes.byref(n))
+        return n.value
+
+
+def register_weight(w_nk: torch.Tensor) -> int:
+    """Register a resident [N, K] bf16 device weight; returns the library handle (TMA descriptors cached)."""
+    _require_cuda(w_nk, "weight")
+    if w_nk.dtype != torch.bfloat16 or w_nk.dim() != 2 or w_nk.stride(1) != 1:
+        raise ValueError("resident weights are [N, K] bf16 with contiguous rows")
+    h = ctypes.c_int64(0)
+    with torch.cuda.device(w_nk.device):
+        _lib.call("npub200_weight_register", ctypes.c_void_p(w_nk.data_ptr()), w_nk.shape[0], w_nk.shape[1],
+                  w_nk.stride(0), ctypes.byref(h))
+    return h.value
+
+
+def release_weight(handle: int) -> None:
+    _lib.call("npub200_weight_release", handle)
+
+
+def _gemm_workspace(x: torch.Tensor, w: torch.Tensor | None, M: int, K: int, N: int) -> torch.Tensor | None:
+    nbytes = ctypes.c_size_t(0)
+    _lib.call("npub200_gemm_workspace_size", ctypes.c_void_p(x.data_ptr()), x.stride(0), M, K,
+              ctypes.c_void_p(w.data_ptr()) if w is not None else None, w.stride(0) if w is not None else 0, N,
+              ctypes.byref(nbytes))
+    if nbytes.value == 0:
+        return None
+    return torch.empty(nbytes.value, dtype=torch.uint8, device=x.device)
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+         out_dtype: torch.dtype = torch.float32, variant: int = 0, handle: int | None = None) -> torch.Tensor:
+    """out[M, N] = x[M, K] @ w[N, K]^T (+ bias) with bf16 operands and f32 accumulation.
+
+    x and w are bf16 CUDA matrices with a unit inner stride (any row stride); bias is bf16 or f32 [N]. With
+    `handle` (from register_weight for this very `w`) the cached weight descriptor is used.
+    """
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("gemm operands must be bf16")
+    if x.dim() != 2 or w.dim() != 2 or x.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("gemm operands must be 2-D with contiguous rows")
+    M, K = x.shape
+    N, K2 = w.shape
+    if K != K2:
+        raise AssertionError(f"K mismatch: x has {K}, weight has {K2}")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=x.device)
+    if out.dtype not in _DT or out.stride(1) != 1 or tuple(out.shape) != (M, N):
+        raise ValueError("out must be an [M, N] bf16/f32 matrix with contiguous rows")
+    if bias is not None:
+        if bias.dtype not in _DT or bias.numel() != N or not bias.is_contiguous():
+            raise ValueError("bias must be a contiguous [N] bf16/f32 vector")
+    ws = _gemm_workspace(x, None if handle is not None else w, M, K, N)
+    args_tail = (ctypes.c_void_p(bias.data_ptr()) if bias is not None else None,
+                 _DT[bias.dtype] if bias is not None else _lib.DTYPE_BF16,
+                 ctypes.c_void_p(out.data_ptr()), out.stride(0), _DT[out.dtype],
+                 ctypes.c_void_p(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
+                 int(variant), ctypes.c_void_p(_stream_ptr(x.device)))
+    with torch.cuda.device(x.device):
+        if handle is not None:
+            _lib.call("npub200_gemm_w", ctypes.c_void_p(x.data_ptr()), x.stride(0), M, K, int(handle), *args_tail)
+        else:
+            _lib.call("npub200_gemm", ctypes.c_void_p(x.data_ptr()), x.stride(0), M, K, ctypes.c_void_p(w.data_ptr()),
+                      w.stride(0), N, *args_tail)
+    return out
+
+
+def _bshd_strides(t: torch.Tensor, head_major: bool) -> tuple[int, int, int]:
+    """(batch, seq, head) element strides of a (B, S, H, D) view given as (B, S, H*D) or (B, H, S, D)."""
+    if head_major:
+        return t.stride(0), t.stride(2), t.stride(1)
+    return t.stride(0), t.stride(1), -1
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
+              head_major_in: bool = False, head_major_out: bool = False, out_dtype: torch.dtype = torch.float32,
+              out: torch.Tensor | None = None, variant: int = 0) -> torch.Tensor:
+    """softmax(q k^T * scale) v for every (batch, head) pair in one launch.
+
+    q/k/v: bf16 CUDA tensors, (B, S, H*D) or (B, H, S, D) when head_major_in; the output (B, Sq, H*D) or
+    (B, H, Sq, D) when head_major_out. Strides may be padded (views), the last dimension must be contiguous.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda(t, name)
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"attention {name} must be bf16")
+        if t.dim() != (4 if head_major_in else 3) or t.stride(-1) != 1:
+            raise ValueError(f"attention {name} must be {'(B, H, S, D)' if head_major_in else '(B, S, H*D)'} with a "
+                             "contiguous last dimension")
+    if head_major_in:
+        B, H, Sq, D = q.shape
+        Skv = k.shape[2]
+        if k.shape != (B, H, Skv, D) or v.shape != (B, H, Skv, D):
+            raise ValueError("k/v shapes do not match q")
+        qs, ks, vs = (_bshd_strides(t, True) for t in (q, k, v))
+    else:
+        B, Sq, inner = q.shape
+        H = int(heads)
+        if H <= 0 or inner % H:
+            raise ValueError(f"q's last dimension {inner} is not a multiple of heads={heads}")
+        D = inner // H
+        Skv = k.shape[1]
+        if k.shape != (B, Skv, inner) or v.shape != (B, Skv, inner):
+            raise ValueError("k/v shapes do not match q")
+        qs, ks, vs = ((t.stride(0), t.stride(1), D) for t in (q, k, v))
+    scale = D ** -0.5 if scale is None else float(scale)
+    if out is None:
+        shape = (B, H, Sq, D) if head_major_out else (B, Sq, H * D)
+        out = torch.empty(shape, dtype=out_dtype, device=q.device)
+    if out.dtype not in _DT or out.stride(-1) != 1:
+        raise ValueError("attention output must be bf16/f32 with a contiguous last dimension")
+    os_ = (out.stride(0), out.stride(2), out.stride(1)) if head_major_out else (out.stride(0), out.stride(1), D)
+    with torch.cuda.device(q.device):
+        _lib.call("npub200_attention",
+                  ctypes.c_void_p(q.data_ptr()), *qs, ctypes.c_void_p(k.data_ptr()), *ks,
+                  ctypes.c_void_p(v.data_ptr()), *vs, ctypes.c_void_p(out.data_ptr()), *os_, _DT[out.dtype],
+                  B, H, Sq, Skv, D, ctypes.c_float(scale), int(variant), ctypes.c_void_p(_stream_ptr(q.device)))
+    return out
+
+
+def status(device: torch.device | int | None = None, clear: bool = True) -> int:
+    """Synchronise the current stream and return the device status bits kernels reported (0 = healthy)."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index or 0))
+    bits = ctypes.c_uint32(0)
+    with torch.cuda.device(dev):
+        _lib.call("npub200_status_read", ctypes.c_void_p(_stream_ptr(dev)), ctypes.byref(bits), 1 if clear else 0)
+    return bits.value
+
+
+def check_status(device: torch.device | int | None = None) -> None:
+    """Raise RuntimeError if a kernel reported a failure (the reference's NpuProgram.wait, xdna1_program.py:475-479)."""
+    bits = status(device)
+    if bits:
+        raise RuntimeError(f"GPU kernel reported failure status 0x{bits:x} (a bounded wait expired)")
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    _lib.call("npub200_set_wait_timeout_ns", ctypes.c_uint64(int(ns)))
+
+
+def set_debug_flags(flags: int) -> None:
+    _lib.call("npub200_set_debug_flags", ctypes.c_uint32(int(flags)))

@@ -1,0 +1,20 @@
+"""CPU oracle for the npu-ai offload hot path. TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline/reference legs may import this package, and
+only as the checker (or the timed CPU baseline), never as the thing measured or shipped. The product path
+(npu_ai_b200) never imports it and has no CPU fallback.
+
+What it restates: the reference's own CPU semantics for the path, i.e. what Tobynau/npu-ai falls back to and
+checks its NPU results against.
+  * GEMM: bf16-rounded x and W multiplied in f32 (scripts/05-gemm-test.py:30, the ComfyUI node's CPU fallback
+    `F.linear`, comfyui/custom_nodes/comfyui_xdna1_npu/__init__.py:151), bias added in f32 after the product
+    (npu/xdna1_gemm.py:417-418).
+  * Attention: scaled dot-product attention in f32 on bf16-rounded q/k/v (scripts/11-attn-fused-test.py:115-119).
+  * aie_numerics: a numpy restatement of the AIE kernel's own arithmetic (npu/kernels/xdna1_attn.cc) used to
+    show how far the reference's NPU numerics sit from the f32 oracle.
+Pinning: tests/golden/ holds fixtures produced by running the reference's CPU fallback code itself
+(tests/golden/make_golden.py imports the reference's ComfyUI node module) and the reference's published
+accuracy figures (docs/02-results.md:709) that the attention oracle reproduces on the reference's own seeded
+inputs; see tests/test_oracle.py.
+"""
+from .reference_ops import attention_ref, bf16_round, cosine, linear_ref, rel_l2_err, rel_max_err  # noqa: F401

@@ -1,0 +1,70 @@
+"""torch-CPU restatement of the reference's CPU semantics (TEST INFRASTRUCTURE ONLY, see oracle/__init__.py)."""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+
+def bf16_round(t: torch.Tensor) -> torch.Tensor:
+    """Round to bf16 (RNE, torch's `.to(bfloat16)` as the reference's to_bf16, npu/xdna1_gemm.py:71-76) and back
+    to f32."""
+    return t.detach().to("cpu").to(torch.bfloat16).float()
+
+
+def linear_ref(x: torch.Tensor, w_nk: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """f32 y = bf16(x) @ bf16(W)^T (+ bias in f32).
+
+    x: (..., K); w_nk: (N, K) in nn.Linear's layout. Follows scripts/05-gemm-test.py:30
+    (`x.to(bf16).float() @ W.to(bf16).float()`, W there given as (K, N)) and the bias add of
+    npu/xdna1_gemm.py:417-418 (f32 bias, after the accumulation). The bias keeps the precision it is given in.
+    """
+    xb = bf16_round(x)
+    wb = bf16_round(w_nk)
+    y = xb.reshape(-1, xb.shape[-1]) @ wb.t()
+    if bias is not None:
+        y = y + bias.detach().to("cpu").float()
+    return y.reshape(*x.shape[:-1], w_nk.shape[0])
+
+
+def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
+                  head_major: bool = False) -> torch.Tensor:
+    """f32 softmax(bf16(q) bf16(k)^T * scale) bf16(v) for every (batch, head) pair.
+
+    q/k/v: (B, S, H*D) (the model's layout) or (B, H, S, D) with head_major. Returns the same layout as the
+    input. Follows scripts/11-attn-fused-test.py:115-119 (SDPA in f32 on bf16-rounded inputs, the reference's
+    "bf16 floor") with the reference runner's default scale d^-0.5 (npu/xdna1_gemm.py:528).
+    """
+    if head_major:
+        B, H, Sq, D = q.shape
+        qh, kh, vh = (bf16_round(t) for t in (q, k, v))
+    else:
+        B, Sq, inner = q.shape
+        H = heads
+        D = inner // H
+        qh, kh, vh = (bf16_round(t).view(B, t.shape[1], H, D).transpose(1, 2) for t in (q, k, v))
+    s = D ** -0.5 if scale is None else float(scale)
+    o = F.scaled_dot_product_attention(qh, kh, vh, scale=s)
+    if head_major:
+        return o
+    return o.transpose(1, 2).reshape(B, Sq, H * D)
+
+
+def rel_max_err(a: torch.Tensor, ref: torch.Tensor) -> float:
+    """max |a - ref| / max |ref|: the reference's accuracy metric (scripts/05-gemm-test.py:37,
+    scripts/11-attn-fused-test.py:49-50, comfyui node :229)."""
+    a = a.detach().float().cpu()
+    ref = ref.detach().float().cpu()
+    return float((a - ref).abs().max() / (ref.abs().max() + 1e-12))
+
+
+def cosine(a: torch.Tensor, ref: torch.Tensor) -> float:
+    """Cosine similarity of the flattened tensors (scripts/05-gemm-test.py:38)."""
+    a = a.detach().double().cpu().reshape(-1)
+    ref = ref.detach().double().cpu().reshape(-1)
+    return float(a @ ref / (a.norm() * ref.norm() + 1e-12))
+
+
+def rel_l2_err(a: torch.Tensor, ref: torch.Tensor) -> float:
+    a = a.detach().double().cpu()
+    ref = ref.detach().double().cpu()
+    return float((a - ref).norm() / (ref.norm() + 1e-30))
