@@ -59,14 +59,21 @@ int npub200_weight_release(int64_t handle);
  * out f32 or bf16. Replaces NpuGemm.matmul_t (npu/xdna1_gemm.py:349-422) and the GEMM mode of the unified NPU
  * program (npu/xdna1_program.py:451-454, npu/kernels/xdna1_attn.cc:480-574). Any M, N, K >= 1: ragged tails are
  * handled in the kernel. x rows need a 16-byte aligned base and ldx % 8 == 0 (TMA); otherwise x is first
- * repacked into `workspace`, which must then hold npub200_gemm_workspace_size() bytes (NULL/0 is fine when that
- * size is 0). `variant` 0 picks the tile automatically, or forces an N tile in {64, 80, 128, 160, 256}.
+ * repacked into `workspace`. Shapes with few output tiles and a long K split K across CTAs, with f32 partials and
+ * per-tile counters in `workspace`. npub200_gemm_workspace_size() gives the bytes the fastest plan uses; its first
+ * bytes hold counters that must be ZERO the first time a workspace is used — the kernels leave them zero, so a
+ * workspace reused on one stream needs zeroing only once (concurrent calls must not share one). A smaller (or
+ * NULL) workspace is accepted when the operands need no repacking: the GEMM then runs without split-K. `variant`
+ * 0 picks the tile automatically, or forces an N tile in {64, 96, 128, 160, 192, 256}.
  * ---------------------------------------------------------------------------------------------------------- */
 int npub200_gemm_workspace_size(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw,
-                                int64_t n, size_t* bytes_out);
+                                int64_t n, int variant, size_t* bytes_out);
 int npub200_gemm(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
                  const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace,
                  size_t workspace_bytes, int variant, void* stream);
+/* The launch plan the library picks for a GEMM shape on the current device: N tile and split-K factor
+ * (the B200 counterpart of NpuGemm.dispatch_shapes, npu/xdna1_gemm.py:295-297, which lists the padded chunks). */
+int npub200_gemm_plan(int64_t m, int64_t n, int64_t k, int variant, int* tile_n_out, int* splits_out);
 /* Same with a registered weight (the resident-weight path the runner uses). */
 int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t weight, const void* bias,
                    int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace, size_t workspace_bytes,

@@ -25,8 +25,10 @@ _SIGNATURES = {
     "npub200_device_sms": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "npub200_weight_register": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, ctypes.POINTER(_c_i64)]),
     "npub200_weight_release": (ctypes.c_int, [_c_i64]),
-    "npub200_gemm_workspace_size": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64,
+    "npub200_gemm_workspace_size": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, ctypes.c_int,
                                                    ctypes.POINTER(ctypes.c_size_t)]),
+    "npub200_gemm_plan": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                         ctypes.POINTER(ctypes.c_int)]),
     "npub200_gemm": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p, ctypes.c_int, _c_p,
                                     _c_i64, ctypes.c_int, _c_p, ctypes.c_size_t, ctypes.c_int, _c_p]),
     "npub200_gemm_w": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, ctypes.c_int, _c_p, _c_i64,

@@ -17,11 +17,14 @@
 //   warp 4      TMA producer: Q once, then K and V tiles into a STAGES-deep ring.
 //   warp 5      TMEM owner + MMA issuer: S[j%2] = Q K_j^T (tcgen05, M=128, N=BN), then O += P_{j-1} V_{j-1}, so the
 //               tensor core computes the next scores while the softmax works on the current ones.
-// Operands use the canonical no-swizzle K-/MN-major layouts (8-row x 16-byte core matrices), filled by TMA one
-// 8-element column chunk at a time from a 4-D (dim, head, seq, batch) tensor map. The head dim is padded to a
-// multiple of 16 (40 -> 48) by TMA's out-of-bounds zero fill; no host padding, no copies of the model's tensors.
+// Data layout: every operand lives in shared memory as 128-byte-swizzled atoms of 64 head-dim (or key) columns,
+// loaded by TMA with 128-byte rows from a 4-D (dim, head, seq, batch) tensor map over the caller's strided
+// tensor. The map's innermost extent is the true head dim, so the columns past it (40 -> 64, 80 -> 128,
+// 160 -> 192) come in as TMA's out-of-bounds zeros: no host padding, no copies of the model's tensors, and the
+// tensor core reads K-major Q/K/P and MN-major V straight from those atoms.
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 
 #include "internal.h"
 
@@ -30,6 +33,7 @@ namespace npub200 {
 constexpr int kAttnBM = 128;
 constexpr int kAttnThreads = 192;
 constexpr int kSoftmaxWarps = 4;
+constexpr int kAtomBytesPerRow = 128;  // one 128-byte swizzle atom row: 64 bf16
 
 struct MapPos {
   int s, h, b;  // position (1..3) of the seq / head / batch dimension in the tensor map
@@ -49,10 +53,13 @@ struct AttnArgs {
 
 template <int DP, int BN, int STAGES>
 struct AttnLayout {
-  static constexpr int kDC = DP / 8;                     // 16-byte column chunks of a row
-  static constexpr int kQBytes = kDC * kAttnBM * 16;
-  static constexpr int kKVBytes = kDC * BN * 16;         // one K (or V) tile
-  static constexpr int kPBytes = kAttnBM * BN * 2;       // one P tile
+  static constexpr int kNA = (DP + 63) / 64;             // 64-column atoms along the head dim
+  static constexpr int kQAtom = kAttnBM * kAtomBytesPerRow;  // 16 KB
+  static constexpr int kKVAtom = BN * kAtomBytesPerRow;
+  static constexpr int kQBytes = kNA * kQAtom;
+  static constexpr int kKVBytes = kNA * kKVAtom;         // one K (or V) tile
+  static constexpr int kPAtoms = BN / 64;                // P: keys along K, 64 per atom
+  static constexpr int kPBytes = kPAtoms * kQAtom;
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQBytes;
   static constexpr int kVOff = kKOff + STAGES * kKVBytes;
@@ -61,30 +68,32 @@ struct AttnLayout {
   // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_empty[2], p_full[2], pv_done[2], drain
   static constexpr int kNumBars = 1 + 3 * STAGES + 8 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kSmemBytes = kMiscOff + 16 + 128;
+  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + slack to align the base to 1 KB
   static constexpr int kSCol = 0;            // S[0] at column 0, S[1] at column BN
   static constexpr int kOCol = 2 * BN;       // O accumulator
   static constexpr int kTmemCols = (2 * BN + DP <= 256) ? 256 : 512;
   static_assert(DP % 16 == 0 && DP >= 16 && DP <= 256, "padded head dim must be a multiple of 16 in [16, 256]");
-  static_assert(BN % 32 == 0 && BN <= 256, "key tile must be a multiple of 32");
+  static_assert(BN % 64 == 0 && BN <= 256, "key tile must be a multiple of 64 (one P atom)");
   static_assert(2 * BN + DP <= 512, "S double buffer + O must fit in 512 TMEM columns");
-  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
-__device__ __forceinline__ void map_coords(const MapPos& p, int chunk, int s, int h, int b, int (&c)[4]) {
-  c[0] = chunk * 8;
-  c[p.s] = s;
-  c[p.h] = h;
-  c[p.b] = b;
+// Coordinates (dim, then the three outer dims in the map's order) of 64-column atom `atom` of row s of (b, h).
+__device__ __forceinline__ void map_coords(const MapPos& p, int atom, int s, int h, int b, int& c0, int& c1, int& c2,
+                                           int& c3) {
+  c0 = atom * 64;
+  c1 = p.s == 1 ? s : (p.h == 1 ? h : b);
+  c2 = p.s == 2 ? s : (p.h == 2 ? h : b);
+  c3 = p.s == 3 ? s : (p.h == 3 ? h : b);
 }
 
 template <int DP, int BN, int STAGES>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSmemBytes <= 113 * 1024) ? 2 : 1)
     attention_fwd_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                                  const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
   using L = AttnLayout<DP, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::kQOff;
   uint8_t* sK = smem + L::kKOff;
   uint8_t* sV = smem + L::kVOff;
@@ -135,6 +144,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
 
   if (warp == 4) {
     // ------------------------------------------------------------------ TMA producer
@@ -142,11 +152,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      int c[4];
+      pdl_wait();  // q/k/v may be the previous kernel's outputs
+      int c0, c1, c2, c3;
       mbar_arrive_expect_tx(q_full, L::kQBytes);
-      for (int ch = 0; ch < L::kDC; ++ch) {
-        map_coords(args.pq, ch, q0, hh, bb, c);
-        tma_load_4d(&tm_q, q_full, sQ + ch * (kAttnBM * 16), c[0], c[1], c[2], c[3]);
+      for (int a = 0; a < L::kNA; ++a) {
+        map_coords(args.pq, a, q0, hh, bb, c0, c1, c2, c3);
+        tma_load_4d(&tm_q, q_full, sQ + a * L::kQAtom, c0, c1, c2, c3);
       }
       int stage = 0;
       uint32_t phase = 0;
@@ -159,14 +170,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         const int kv0 = j * BN;
         mbar_arrive_expect_tx(&k_full[stage], L::kKVBytes);
-        for (int ch = 0; ch < L::kDC; ++ch) {
-          map_coords(args.pk, ch, kv0, hh, bb, c);
-          tma_load_4d(&tm_k, &k_full[stage], sK + stage * L::kKVBytes + ch * (BN * 16), c[0], c[1], c[2], c[3]);
+        for (int a = 0; a < L::kNA; ++a) {
+          map_coords(args.pk, a, kv0, hh, bb, c0, c1, c2, c3);
+          tma_load_4d(&tm_k, &k_full[stage], sK + stage * L::kKVBytes + a * L::kKVAtom, c0, c1, c2, c3);
         }
         mbar_arrive_expect_tx(&v_full[stage], L::kKVBytes);
-        for (int ch = 0; ch < L::kDC; ++ch) {
-          map_coords(args.pv, ch, kv0, hh, bb, c);
-          tma_load_4d(&tm_v, &v_full[stage], sV + stage * L::kKVBytes + ch * (BN * 16), c[0], c[1], c[2], c[3]);
+        for (int a = 0; a < L::kNA; ++a) {
+          map_coords(args.pv, a, kv0, hh, bb, c0, c1, c2, c3);
+          tma_load_4d(&tm_v, &v_full[stage], sV + stage * L::kKVBytes + a * L::kKVAtom, c0, c1, c2, c3);
         }
         ++issued;
         if (++stage == STAGES) {
@@ -218,10 +229,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t va = v_addr + st * L::kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          // P: K-major, core matrices 8 rows x 16 B; 8-key chunks kAttnBM*16 bytes apart.
-          const uint64_t a = smem_desc_interleaved(pa + kk * 2 * (kAttnBM * 16), kAttnBM * 16, 128);
-          // V: MN-major (head dim contiguous): 8-key groups 128 B apart (LBO), 8-dim chunks BN*16 B apart (SBO).
-          const uint64_t b = smem_desc_interleaved(va + kk * 256, 128, BN * 16);
+          // P: K-major over keys, atoms of 64 keys, +32 B per 16 keys inside an atom.
+          const uint64_t a = smem_desc_kmajor_sw128(pa + (kk >> 2) * L::kQAtom + (kk & 3) * 32);
+          // V: MN-major (head dim contiguous), 16 keys = 16 rows of 128 B further per K step.
+          const uint64_t b = smem_desc_mnmajor_sw128(va + kk * 16 * kAtomBytesPerRow, L::kKVAtom);
           umma_f16_ss(tmem_base + L::kOCol, a, b, kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&pv_done[buf]);
@@ -245,8 +256,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t ka = k_addr + st * L::kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < DP / 16; ++kk) {
-          const uint64_t a = smem_desc_interleaved(q_addr + kk * 2 * (kAttnBM * 16), kAttnBM * 16, 128);
-          const uint64_t b = smem_desc_interleaved(ka + kk * 2 * (BN * 16), BN * 16, 128);
+          // Q and K: K-major over the head dim, atoms of 64 columns, +32 B per 16 columns inside an atom.
+          const uint64_t a = smem_desc_kmajor_sw128(q_addr + (kk >> 2) * L::kQAtom + (kk & 3) * 32);
+          const uint64_t b = smem_desc_kmajor_sw128(ka + (kk >> 2) * L::kKVAtom + (kk & 3) * 32);
           umma_f16_ss(tmem_base + L::kSCol + buf * BN, a, b, kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[buf]);
@@ -258,7 +270,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (ok && nkv >= 1 && !issue_pv(nkv - 1)) ok = false;
       if (!ok) {
         umma_commit(drain);
-        mbar_wait_drain(drain, (args.ctl.debug & 1u) ? 0u : 0u, args.ctl);
+        mbar_wait_drain(drain, 0u, args.ctl);
       }
     }
   } else {
@@ -276,15 +288,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         break;
       }
       tc_fence_after();
-      float s[BN];
+      float s[BN];  // raw scores of this row (the scale is folded into the exponent below)
 #pragma unroll
       for (int cc = 0; cc < BN; cc += 32) {
         uint32_t r[32];
         tmem_ld32(lane_base + uint32_t(L::kSCol + buf * BN + cc), r);
-        tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; ++t) s[cc + t] = __uint_as_float(r[t]) * c;
+        for (int t = 0; t < 32; ++t) s[cc + t] = __uint_as_float(r[t]);
       }
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[buf]);
@@ -295,14 +307,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int t = 0; t < BN; ++t)
           if (kv0 + t >= args.Skv) s[t] = -INFINITY;
       }
-      float mx = s[0];
+      // Row max as 8 independent chains, then a 3-level tree (short dependency chains keep the pipes busy).
+      float mx8[8];
 #pragma unroll
-      for (int t = 1; t < BN; ++t) mx = fmaxf(mx, s[t]);
+      for (int e = 0; e < 8; ++e) mx8[e] = s[e];
+#pragma unroll
+      for (int t = 8; t < BN; t += 8)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx8[e] = fmaxf(mx8[e], s[t + e]);
+#pragma unroll
+      for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+        for (int e = 0; e < w; ++e) mx8[e] = fmaxf(mx8[e], mx8[e + w]);
+      const float mx = mx8[0] * c;  // log2 units (c = scale * log2 e > 0)
       // Lazy running max: move only when this tile's max beats it by more than the threshold.
       const bool move = mx > m + args.rescale_thr;
       const float m_new = move ? mx : m;
       const float alpha = fast_exp2(m - m_new);  // 1 when unchanged, 0 on the first tile
-      float rowsum = 0.0f;
+      const float neg_m = -m_new;
+      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       // P buffer `buf` is free once PV of tile j-2 has completed.
       if (j >= 2 &&
           !mbar_wait_bounded(&pv_done[buf], (uint32_t((j - 2) >> 1) & 1u), abort_flag, args.ctl,
@@ -310,23 +333,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ok = false;
         break;
       }
-      uint8_t* prow = sP + buf * L::kPBytes + row * 16;
+      // P row: 16-byte chunks of 8 keys, chunk q of an atom stored at (q ^ row % 8) (the 128-byte swizzle).
+      uint8_t* prow = sP + buf * L::kPBytes + row * kAtomBytesPerRow;
 #pragma unroll
       for (int ch = 0; ch < BN / 8; ++ch) {
         float p[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          p[e] = fast_exp2(s[ch * 8 + e] - m_new);
-          rowsum += p[e];
+          p[e] = fast_exp2(fmaf(s[ch * 8 + e], c, neg_m));
+          rs8[e] += p[e];
         }
         uint4 v;
         v.x = pack_bf16x2(p[0], p[1]);
         v.y = pack_bf16x2(p[2], p[3]);
         v.z = pack_bf16x2(p[4], p[5]);
         v.w = pack_bf16x2(p[6], p[7]);
-        *reinterpret_cast<uint4*>(prow + ch * (kAttnBM * 16)) = v;
+        *reinterpret_cast<uint4*>(prow + (ch >> 3) * L::kQAtom + (((ch & 7) ^ (row & 7)) << 4)) = v;
       }
-      l = l * alpha + rowsum;
+#pragma unroll
+      for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+        for (int e = 0; e < w; ++e) rs8[e] += rs8[e + w];
+      l = l * alpha + rs8[0];
       m = m_new;
       // O correction (rare with the lazy max): O_row *= alpha once PV of tile j-1 has landed. Warp-uniform because
       // tcgen05.ld/st are warp-wide; lanes whose max did not move scale by 1.
@@ -355,6 +383,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     if (ok && nkv >= 1) {
       const int last = nkv - 1;
+      pdl_wait();  // the previous kernel may still read the output buffer
       if (mbar_wait_bounded(&pv_done[last & 1], uint32_t(last >> 1) & 1u, abort_flag, args.ctl,
                             kStatusTimeoutEpilogue)) {
         tc_fence_after();
@@ -379,7 +408,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 for (int t = 0; t < 4; ++t)
                   reinterpret_cast<float4*>(dst)[t] = make_float4(o[4 * t], o[4 * t + 1], o[4 * t + 2], o[4 * t + 3]);
               } else {
-                for (int t = 0; t < ncols; ++t) dst[t] = o[t];
+#pragma unroll
+                for (int t = 0; t < 16; ++t)
+                  if (t < ncols) dst[t] = o[t];
               }
             } else {
               __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(args.out) + obase + cc;
@@ -398,10 +429,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                   v1.w = pack_bf16x2(o[14], o[15]);
                   reinterpret_cast<uint4*>(dst)[1] = v1;
                 } else {
-                  for (int t = 8; t < ncols; ++t) dst[t] = __float2bfloat16_rn(o[t]);
+#pragma unroll
+                  for (int t = 8; t < 16; ++t)
+                    if (t < ncols) dst[t] = __float2bfloat16_rn(o[t]);
                 }
               } else {
-                for (int t = 0; t < ncols; ++t) dst[t] = __float2bfloat16_rn(o[t]);
+#pragma unroll
+                for (int t = 0; t < 16; ++t)
+                  if (t < ncols) dst[t] = __float2bfloat16_rn(o[t]);
               }
             }
           }
@@ -429,7 +464,8 @@ struct DimStride {
   int which;       // 0 = seq, 1 = head, 2 = batch
 };
 
-// 4-D map (dim, then seq/head/batch sorted by stride) with a box of 8 dim-elements x `rows` sequence rows.
+// 4-D map (dim, then seq/head/batch sorted by stride) with a box of 64 dim-elements (one 128-byte swizzle atom) x
+// `rows` sequence rows. The dim extent is the true head dim: the columns of the atom past it read as zeros.
 int encode_bshd_map(const void* base, int64_t D, int64_t S, int64_t H, int64_t B, int64_t ss, int64_t sh, int64_t sb,
                     int rows, CUtensorMap* out, MapPos* pos) {
   EncodeTiledFn enc = nullptr;
@@ -447,7 +483,7 @@ int encode_bshd_map(const void* base, int64_t D, int64_t S, int64_t H, int64_t B
   std::sort(d, d + 3, [](const DimStride& a, const DimStride& b) { return a.stride < b.stride; });
   cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(d[0].extent), cuuint64_t(d[1].extent), cuuint64_t(d[2].extent)};
   cuuint64_t strides[3] = {cuuint64_t(d[0].stride) * 2, cuuint64_t(d[1].stride) * 2, cuuint64_t(d[2].stride) * 2};
-  cuuint32_t box[4] = {8, 1, 1, 1};
+  cuuint32_t box[4] = {64, 1, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   for (int i = 0; i < 3; ++i) {
     if (d[i].which == 0) {
@@ -460,7 +496,7 @@ int encode_bshd_map(const void* base, int64_t D, int64_t S, int64_t H, int64_t B
     }
   }
   CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(kErrInvalid, "cuTensorMapEncodeTiled failed (%d) for an attention operand (D=%lld S=%lld H=%lld B=%lld)",
@@ -479,8 +515,54 @@ int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(attention smem)");
     configured[device] = true;
   }
-  kern<<<grid, kAttnThreads, L::kSmemBytes, st>>>(mq, mk, mv, a);
-  return check_cuda(cudaGetLastError(), "attention kernel launch");
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = L::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, a), "attention kernel launch");
+}
+
+// Kernel variant for a padded head dim and key tile (64 or 128 keys per tile).
+int launch_for(int64_t DP, int BN, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+               const AttnArgs& a, dim3 grid, cudaStream_t st, int dev) {
+#define NPUB200_ATTN_CASE(dp, bn, stages) \
+  if (DP == dp && BN == bn) return launch_attn<dp, bn, stages>(mq, mk, mv, a, grid, st, dev);
+  // one 64-column atom of head dim (d <= 64)
+  NPUB200_ATTN_CASE(16, 64, 3)
+  NPUB200_ATTN_CASE(32, 64, 3)
+  NPUB200_ATTN_CASE(48, 64, 3)
+  NPUB200_ATTN_CASE(64, 64, 3)
+  NPUB200_ATTN_CASE(16, 128, 3)
+  NPUB200_ATTN_CASE(32, 128, 3)
+  NPUB200_ATTN_CASE(48, 128, 3)
+  NPUB200_ATTN_CASE(64, 128, 3)
+  // two atoms (64 < d <= 128)
+  NPUB200_ATTN_CASE(80, 64, 3)
+  NPUB200_ATTN_CASE(96, 64, 3)
+  NPUB200_ATTN_CASE(112, 64, 3)
+  NPUB200_ATTN_CASE(128, 64, 3)
+  NPUB200_ATTN_CASE(80, 128, 2)
+  NPUB200_ATTN_CASE(96, 128, 2)
+  NPUB200_ATTN_CASE(112, 128, 2)
+  NPUB200_ATTN_CASE(128, 128, 2)
+  // three or four atoms (128 < d <= 256): 64-key tiles only (TMEM: 2 x 64 S columns + d O columns)
+  NPUB200_ATTN_CASE(144, 64, 2)
+  NPUB200_ATTN_CASE(160, 64, 2)
+  NPUB200_ATTN_CASE(176, 64, 2)
+  NPUB200_ATTN_CASE(192, 64, 2)
+  NPUB200_ATTN_CASE(208, 64, 2)
+  NPUB200_ATTN_CASE(224, 64, 2)
+  NPUB200_ATTN_CASE(240, 64, 2)
+  NPUB200_ATTN_CASE(256, 64, 2)
+#undef NPUB200_ATTN_CASE
+  return fail(kErrUnsupported, "no attention variant for padded head dim %lld with %d-key tiles", (long long)DP, BN);
 }
 
 }  // namespace
@@ -497,7 +579,11 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   for (const void* ptr : {p.q, p.k, p.v})
     if (reinterpret_cast<uintptr_t>(ptr) & 15u) return fail(kErrInvalid, "q/k/v base addresses must be 16-byte aligned");
   const int64_t DP = (p.D + 15) / 16 * 16;
-  const int BN = DP > 128 ? 64 : 128;
+  // Key tile (variant): 128 keys per tile by default; 64 keys halves the per-CTA footprint (two CTAs share an SM
+  // when it fits) and is the only tile for head dims above 128.
+  int BN = p.variant ? p.variant : 128;
+  if (BN != 64 && BN != 128) return fail(kErrUnsupported, "attention key tile %d (variants: 64, 128)", BN);
+  if (DP > 128) BN = 64;
 
   CUtensorMap mq, mk, mv;
   AttnArgs a;
@@ -522,25 +608,7 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   a.ctl.debug = p.debug;
   const dim3 grid(unsigned((p.Sq + kAttnBM - 1) / kAttnBM), unsigned(pairs));
   if (grid.x > 0x7fffffffu) return fail(kErrInvalid, "too many query tiles");
-  switch (DP) {
-    case 16: return launch_attn<16, 128, 3>(mq, mk, mv, a, grid, stream, dev->device);
-    case 32: return launch_attn<32, 128, 3>(mq, mk, mv, a, grid, stream, dev->device);
-    case 48: return launch_attn<48, 128, 3>(mq, mk, mv, a, grid, stream, dev->device);
-    case 64: return launch_attn<64, 128, 3>(mq, mk, mv, a, grid, stream, dev->device);
-    case 80: return launch_attn<80, 128, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 96: return launch_attn<96, 128, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 112: return launch_attn<112, 128, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 128: return launch_attn<128, 128, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 144: return launch_attn<144, 64, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 160: return launch_attn<160, 64, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 176: return launch_attn<176, 64, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 192: return launch_attn<192, 64, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 208: return launch_attn<208, 64, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 224: return launch_attn<224, 64, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 240: return launch_attn<240, 64, 2>(mq, mk, mv, a, grid, stream, dev->device);
-    case 256: return launch_attn<256, 64, 2>(mq, mk, mv, a, grid, stream, dev->device);
-  }
-  return fail(kErrUnsupported, "no attention variant for head dim %lld", (long long)p.D);
+  return launch_for(DP, BN, mq, mk, mv, a, grid, stream, dev->device);
 }
 
 }  // namespace npub200

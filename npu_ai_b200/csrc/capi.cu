@@ -8,7 +8,7 @@
 #include <mutex>
 #include <unordered_map>
 
-#include "../../include/npu_b200.h"
+#include "npu_b200.h"
 #include "internal.h"
 
 namespace npub200 {
@@ -112,13 +112,33 @@ bool tma_rows_ok(const void* p, int64_t ld, int64_t cols) { return aligned16(p) 
 
 int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
-size_t gemm_ws_bytes(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n) {
+// Workspace layout: [split-K region: zeroed tile counters + f32 partials][repacked x][repacked W].
+struct WsLayout {
+  size_t split_bytes = 0;
+  size_t x_off = 0, x_bytes = 0;
+  size_t w_off = 0, w_bytes = 0;
+  size_t total = 0;
+};
+
+WsLayout gemm_ws_layout(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                        int variant, int sms) {
+  WsLayout L;
   const int64_t kp = round_up(k, 8);
-  size_t bytes = 0;
   const bool pad_k = (k % 8) != 0;
-  if (pad_k || !tma_rows_ok(x, ldx, k)) bytes += size_t(round_up(m * kp * 2, 256));
-  if (w != nullptr && (pad_k || !tma_rows_ok(w, ldw, k))) bytes += size_t(round_up(n * kp * 2, 256));
-  return bytes;
+  L.split_bytes = sms > 0 ? gemm_plan(m, n, kp, sms, variant).split_ws_bytes : 0;
+  size_t off = L.split_bytes;
+  if (pad_k || !tma_rows_ok(x, ldx, k)) {
+    L.x_off = off;
+    L.x_bytes = size_t(round_up(m * kp * 2, 256));
+    off += L.x_bytes;
+  }
+  if (w != nullptr && (pad_k || !tma_rows_ok(w, ldw, k))) {
+    L.w_off = off;
+    L.w_bytes = size_t(round_up(n * kp * 2, 256));
+    off += L.w_bytes;
+  }
+  L.total = off;
+  return L;
 }
 
 int check_gemm_common(int64_t m, int64_t k, int64_t n, int bias_dtype, const void* out, int64_t ldo,
@@ -160,34 +180,37 @@ int gemm_common(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w,
   p.w_map_cache = w_map;
   p.debug = g_debug_flags.load();
 
+  const DeviceInfo* dev = nullptr;
+  if (int rc = current_device_info(&dev)) return rc;
   const bool pad_k = (k % 8) != 0;
   const bool x_ok = !pad_k && tma_rows_ok(x, ldx, k);
   const bool w_ok = !pad_k && tma_rows_ok(w, ldw, k);
+  const WsLayout L = gemm_ws_layout(x, ldx, m, k, w_map ? nullptr : w, ldw, n, variant, dev->sms);
+  if (workspace != nullptr && !aligned16(workspace)) return fail(kErrInvalid, "workspace must be 16-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int64_t kp = round_up(k, 8);
   if (!x_ok || !w_ok) {
-    // Workspace path: dense copies with K padded to a multiple of 8 (zero columns add nothing to the dot products).
-    const size_t need = gemm_ws_bytes(x, ldx, m, k, w, ldw, n);
-    if (workspace == nullptr || workspace_bytes < need)
+    // Repack path: dense copies with K padded to a multiple of 8 (zero columns add nothing to the dot products).
+    if (ws == nullptr || workspace_bytes < L.total)
       return fail(kErrInvalid, "this GEMM needs a %zu-byte workspace (operands are not TMA-addressable), got %zu",
-                  need, workspace_bytes);
-    if (!aligned16(workspace)) return fail(kErrInvalid, "workspace must be 16-byte aligned");
-    const int64_t kp = round_up(k, 8);
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
+                  L.total, workspace_bytes);
     if (!x_ok) {
-      if (int rc = repack_rows_bf16(x, ldx, m, k, ws, kp, st)) return rc;
-      p.x = ws;
+      if (int rc = repack_rows_bf16(x, ldx, m, k, ws + L.x_off, kp, st)) return rc;
+      p.x = ws + L.x_off;
       p.ldx = kp;
-      ws += round_up(m * kp * 2, 256);
     }
     if (!w_ok) {
-      if (int rc = repack_rows_bf16(w, ldw, n, k, ws, kp, st)) return rc;
-      p.w = ws;
+      if (int rc = repack_rows_bf16(w, ldw, n, k, ws + L.w_off, kp, st)) return rc;
+      p.w = ws + L.w_off;
       p.ldw = kp;
       p.w_map_cache = nullptr;
     }
-    if (pad_k) {
-      p.K = kp;
-      if (x_ok) return fail(kErrInvalid, "internal: K padding requires a repacked x");
-    }
+    if (pad_k) p.K = kp;
+  }
+  // Split-K partials and counters (optional: without room for them the kernel runs one CTA per tile).
+  if (ws != nullptr && L.split_bytes > 0 && workspace_bytes >= L.split_bytes) {
+    p.ws_split = ws;
+    p.ws_split_bytes = L.split_bytes;
   }
   return gemm_launch(p, st);
 }
@@ -237,9 +260,22 @@ int npub200_weight_release(int64_t handle) {
 }
 
 int npub200_gemm_workspace_size(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw,
-                                int64_t n, size_t* bytes_out) {
+                                int64_t n, int variant, size_t* bytes_out) {
   if (bytes_out == nullptr) return fail(kErrInvalid, "null output pointer");
-  *bytes_out = gemm_ws_bytes(x, ldx, m, k, w, ldw, n);
+  if (m <= 0 || k <= 0 || n <= 0) return fail(kErrInvalid, "GEMM sizes must be positive");
+  const DeviceInfo* d = nullptr;
+  if (int rc = current_device_info(&d)) return rc;
+  *bytes_out = gemm_ws_layout(x, ldx, m, k, w, ldw, n, variant, d->sms).total;
+  return kOk;
+}
+
+int npub200_gemm_plan(int64_t m, int64_t n, int64_t k, int variant, int* tile_n_out, int* splits_out) {
+  if (m <= 0 || n <= 0 || k <= 0) return fail(kErrInvalid, "GEMM sizes must be positive");
+  const DeviceInfo* d = nullptr;
+  if (int rc = current_device_info(&d)) return rc;
+  const GemmPlan plan = gemm_plan(m, n, round_up(k, 8), d->sms, variant);
+  if (tile_n_out) *tile_n_out = plan.bn;
+  if (splits_out) *splits_out = plan.splits;
   return kOk;
 }
 
@@ -272,7 +308,7 @@ int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t wei
     if (int rc = current_device_info(&d)) return rc;
     if (d->device != e.device) return fail(kErrInvalid, "weight was registered on device %d, current is %d",
                                            e.device, d->device);
-    const int bn = variant ? variant : gemm_pick_bn(m, n, k, d->sms);
+    const int bn = gemm_plan(m, n, k, d->sms, variant).bn;
     auto mit = e.maps.find(bn);
     if (mit == e.maps.end()) {
       CUtensorMap fresh;

@@ -15,6 +15,7 @@
 // dense matrix); anything else is repacked by the host into a caller-provided workspace first.
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 
 #include "internal.h"
 
@@ -32,6 +33,13 @@ struct GemmArgs {
   void* out;
   long long ldo;
   int out_f32;
+  int tma_store;  // 1: the output goes out through TMA stores (aligned output), 0: direct predicated stores
+  // Split-K: `splits` CTAs share an output tile, each over `kb_per_split` K blocks; f32 partials go to
+  // `ws_partial` ([tile][split][column][row]) and the last to arrive (ticket from `ws_counter[tile]`, which it
+  // resets to 0) sums them in split order, so the result does not depend on arrival order.
+  int splits, kb_per_split;
+  float* ws_partial;
+  unsigned int* ws_counter;
   KernelCtl ctl;
 };
 
@@ -41,61 +49,93 @@ struct GemmLayout {
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
+  // Epilogue staging: per epilogue warp two 32-row x 128-byte tiles (128-byte swizzle) for the TMA stores.
+  static constexpr int kStagingOffset = STAGES * kStageBytes;
+  static constexpr int kStagingBytes = 4 * 2 * 32 * 128;
+  static constexpr int kBarOffset = kStagingOffset + kStagingBytes;
   static constexpr int kNumBars = 2 * STAGES + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], drain
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOffset + 16 + 1024;  // + slack to align the base to 1 KB
   static_assert(kBBytes % 1024 == 0, "B stage must keep 1 KB alignment for the 128-byte swizzle");
-  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 is a multiple of 16 in [16, 256]");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "N tile: a multiple of 32 (UMMA N for M=128 <= 256)");
+  static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
 };
 
-__device__ __forceinline__ float bias_at(const GemmArgs& a, int col) {
-  return a.bias_f32 ? __ldg(static_cast<const float*>(a.bias) + col)
-                    : __bfloat162float(static_cast<const __nv_bfloat16*>(a.bias)[col]);
-}
-
-// Store 16 consecutive accumulator columns of one output row (columns gcol .. gcol+15, rows/cols predicated).
-__device__ __forceinline__ void store_row16(const GemmArgs& a, int grow, int gcol, const uint32_t (&r)[16]) {
-  if (grow >= a.M) return;
-  float v[16];
+// Bias for 32 consecutive output columns starting at gcol (0 beyond N). Compile-time indices only, so the values
+// stay in registers; the loads are broadcasts (every thread of the warp reads the same addresses).
+__device__ __forceinline__ void load_bias32(const GemmArgs& a, int gcol, float (&b)[32]) {
+  if (a.bias == nullptr) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-  const int ncols = min(16, a.N - gcol);
-  if (ncols <= 0) return;
-  if (a.bias != nullptr) {
-    if (ncols == 16) {
+    for (int j = 0; j < 32; ++j) b[j] = 0.0f;
+    return;
+  }
+  if (a.bias_f32) {
+    const float* p = static_cast<const float*>(a.bias) + gcol;
+    if (gcol + 32 <= a.N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] += bias_at(a, gcol + j);
+      for (int j = 0; j < 8; ++j) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(p) + j);
+        b[4 * j] = t.x;
+        b[4 * j + 1] = t.y;
+        b[4 * j + 2] = t.z;
+        b[4 * j + 3] = t.w;
+      }
     } else {
-      for (int j = 0; j < ncols; ++j) v[j] += bias_at(a, gcol + j);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) b[j] = (gcol + j < a.N) ? __ldg(p + j) : 0.0f;
+    }
+  } else {
+    const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(a.bias) + gcol;
+    if (gcol + 32 <= a.N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 t = __ldg(reinterpret_cast<const uint4*>(p) + j);
+        const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          b[8 * j + 2 * e] = __uint_as_float(w[e] << 16);
+          b[8 * j + 2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) b[j] = (gcol + j < a.N) ? __bfloat162float(p[j]) : 0.0f;
     }
   }
+}
+
+// Direct-store epilogue for outputs TMA cannot address: 32 columns of one row, rows/columns predicated with
+// compile-time indices (no dynamically indexed arrays, so nothing spills to local memory).
+__device__ __forceinline__ void store_row32_direct(const GemmArgs& a, int grow, int gcol, const float (&v)[32]) {
+  if (grow >= a.M || gcol >= a.N) return;
+  const bool full = gcol + 32 <= a.N;
   if (a.out_f32) {
     float* o = static_cast<float*>(a.out) + (long long)grow * a.ldo + gcol;
-    if (ncols == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-      float4* o4 = reinterpret_cast<float4*>(o);
+    if (full && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      for (int j = 0; j < 8; ++j)
+        reinterpret_cast<float4*>(o)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     } else {
-      for (int j = 0; j < ncols; ++j) o[j] = v[j];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (gcol + j < a.N) o[j] = v[j];
     }
   } else {
     __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + (long long)grow * a.ldo + gcol;
-    if (ncols == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-      uint4 p0, p1;
-      p0.x = pack_bf16x2(v[0], v[1]);
-      p0.y = pack_bf16x2(v[2], v[3]);
-      p0.z = pack_bf16x2(v[4], v[5]);
-      p0.w = pack_bf16x2(v[6], v[7]);
-      p1.x = pack_bf16x2(v[8], v[9]);
-      p1.y = pack_bf16x2(v[10], v[11]);
-      p1.z = pack_bf16x2(v[12], v[13]);
-      p1.w = pack_bf16x2(v[14], v[15]);
-      uint4* o4 = reinterpret_cast<uint4*>(o);
-      o4[0] = p0;
-      o4[1] = p1;
+    if (full && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 t;
+        t.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
+        t.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+        t.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+        t.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+        reinterpret_cast<uint4*>(o)[j] = t;
+      }
     } else {
-      for (int j = 0; j < ncols; ++j) o[j] = __float2bfloat16_rn(v[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (gcol + j < a.N) o[j] = __float2bfloat16_rn(v[j]);
     }
   }
 }
@@ -103,7 +143,7 @@ __device__ __forceinline__ void store_row16(const GemmArgs& a, int grow, int gco
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                             const GemmArgs args) {
+                             const __grid_constant__ CUtensorMap tm_out, const GemmArgs args) {
   using L = GemmLayout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -146,8 +186,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Let the next kernel on the stream start its prologue on idle SMs; it waits for this grid before reading.
+  pdl_launch_dependents();
 
-  const int num_tiles = args.num_tiles;
+  const int num_units = args.num_tiles * args.splits;
   const int num_m = args.num_m_blk;
   const int num_kb = args.num_kb;
 
@@ -158,10 +200,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      pdl_wait();  // x may be the previous kernel's output
+      for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+        const int tile = unit / args.splits;
         const int m0 = (tile % num_m) * kGemmBM;
         const int n0 = (tile / num_m) * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb_begin = (unit % args.splits) * args.kb_per_split;
+        const int kb_end = min(num_kb, kb_begin + args.kb_per_split);
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutProducer)) {
             ok = false;
             break;
@@ -203,7 +249,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!mbar_wait_bounded(drain, 0, abort_flag, args.ctl, kStatusForced)) ok = false;
       }
       int local = 0;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
+      for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutMma)) {
@@ -212,7 +258,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb_begin = (unit % args.splits) * args.kb_per_split;
+        const int kb_end = min(num_kb, kb_begin + args.kb_per_split);
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.ctl, kStatusTimeoutMma)) {
             ok = false;
             break;
@@ -223,7 +271,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; ++k) {
             // +32 bytes per K step of 16 bf16 inside the swizzle atom (descriptor address field is >> 4).
-            umma_f16_ss(d_tmem, a_desc + 2u * k, b_desc + 2u * k, kIdesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_ss(d_tmem, a_desc + 2u * k, b_desc + 2u * k, kIdesc, (kb > kb_begin || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);  // frees the smem stage once these MMAs have read it
           if (++stage == STAGES) {
@@ -244,26 +292,128 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int quarter = warp & 3;  // TMEM lanes this warp may access: [32*quarter, 32*quarter + 32)
     const int row = quarter * 32 + lane;
+    // Output goes out in chunks of 128-byte rows (64 bf16 or 32 f32 columns) through a double-buffered staging
+    // tile per warp, laid out with the 128-byte swizzle so the row-per-thread writes hit distinct banks. A chunk
+    // that would reach past the tile (BN not a multiple of the chunk) is written with direct stores instead.
+    uint8_t* staging = smem + L::kStagingOffset + (warp - 2) * (2 * 32 * 128);
+    volatile int* last_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 8);
+    const int cw = args.out_f32 ? 32 : 64;
+    const int splits = args.splits;
+    int chunk_no = 0;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    pdl_wait();  // the previous kernel may still read (or write) the output / bias
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.ctl, kStatusTimeoutEpilogue)) break;
       tc_fence_after();
+      const int tile = unit / splits;
+      const int split = unit % splits;
       const int m0 = (tile % num_m) * kGemmBM;
       const int n0 = (tile / num_m) * BN;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+      bool emit = true;
+      if (splits > 1) {
+        // Publish this split's partial, then take a ticket; the last split of the tile reduces.
+        float* mine = args.ws_partial + (size_t(tile) * splits + split) * BN * kGemmBM;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(t_row + uint32_t(c), r);
-        tmem_wait_ld();
-        store_row16(args, m0 + row, n0 + c, r);
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_row + uint32_t(c), r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) __stcg(mine + (c + j) * kGemmBM + row, __uint_as_float(r[j]));
+        }
+        __threadfence();
+        named_barrier_sync(1, 128);
+        if (threadIdx.x == 64) {
+          const unsigned int ticket = atomicAdd(args.ws_counter + tile, 1u);
+          *last_flag = (ticket == unsigned(splits - 1)) ? 1 : 0;
+        }
+        named_barrier_sync(1, 128);
+        emit = *last_flag != 0;
+        __threadfence();
+      }
+      if (emit) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += cw) {
+          const bool chunk_tma = args.tma_store && c0 + cw <= BN;
+          uint8_t* sb = staging + (chunk_no & 1) * (32 * 128);
+          if (chunk_tma) {
+            if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
+            __syncwarp();
+          }
+#pragma unroll 1
+          for (int c = c0; c < min(c0 + cw, BN); c += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_row + uint32_t(c), r);
+            float b[32];
+            load_bias32(args, n0 + c, b);
+            tmem_wait_ld();
+            float v[32];
+            if (splits > 1) {
+              // Fixed summation order over the splits, this split's own partial taken from TMEM.
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+              for (int sp = 0; sp < splits; ++sp) {
+                if (sp == split) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r[j]);
+                } else {
+                  const float* part = args.ws_partial + (size_t(tile) * splits + sp) * BN * kGemmBM;
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] += __ldcg(part + (c + j) * kGemmBM + row);
+                }
+              }
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += b[j];
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + b[j];
+            }
+            if (chunk_tma) {
+              uint8_t* rowp = sb + lane * 128;
+              if (args.out_f32) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int phys = j ^ (lane & 7);
+                  *reinterpret_cast<float4*>(rowp + phys * 16) =
+                      make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                }
+              } else {
+                const int chunk0 = ((c - c0) * 2) / 16;  // 16-byte chunk index of this column group in the row
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  uint4 t;
+                  t.x = pack_bf16x2(v[8 * j], v[8 * j + 1]);
+                  t.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+                  t.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+                  t.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+                  const int phys = (chunk0 + j) ^ (lane & 7);
+                  *reinterpret_cast<uint4*>(rowp + phys * 16) = t;
+                }
+              }
+            } else {
+              store_row32_direct(args, m0 + row, n0 + c, v);
+            }
+          }
+          if (chunk_tma) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && n0 + c0 < args.N && m0 + quarter * 32 < args.M) {
+              tma_store_2d(&tm_out, sb, n0 + c0, m0 + quarter * 32);
+              bulk_commit();
+            }
+            ++chunk_no;
+          }
+        }
+        if (splits > 1 && threadIdx.x == 64) args.ws_counter[tile] = 0u;  // leave the counter zeroed for reuse
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
+    if (args.tma_store && lane == 0) bulk_wait_read<0>();  // staging must not be released while being read
   }
 
   __syncthreads();
@@ -279,8 +429,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 namespace {
 
 template <int BN, int STAGES>
-int launch_variant(const CUtensorMap& mx, const CUtensorMap& mw, const GemmArgs& args, int grid, cudaStream_t st,
-                   int device) {
+int launch_variant(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mo, const GemmArgs& args,
+                   int grid, cudaStream_t st, int device) {
   using L = GemmLayout<BN, STAGES>;
   static bool configured[64] = {false};
   auto kern = gemm_bf16_tcgen05_kernel<BN, STAGES>;
@@ -290,8 +440,18 @@ int launch_variant(const CUtensorMap& mx, const CUtensorMap& mw, const GemmArgs&
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm smem)");
     configured[device] = true;
   }
-  kern<<<grid, kGemmThreads, L::kSmemBytes, st>>>(mx, mw, args);
-  return check_cuda(cudaGetLastError(), "gemm kernel launch");
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = L::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, mx, mw, mo, args), "gemm kernel launch");
 }
 
 int encode_kmajor_map(const void* base, int64_t rows, int64_t k, int64_t ld, int box_rows, CUtensorMap* out) {
@@ -310,31 +470,72 @@ int encode_kmajor_map(const void* base, int64_t rows, int64_t k, int64_t ld, int
   return kOk;
 }
 
-constexpr int kTileChoices[] = {64, 80, 128, 160, 256};
+// Output map for the TMA-store epilogue: boxes of 32 rows x 128 bytes (64 bf16 or 32 f32), 128-byte swizzle.
+int encode_out_map(void* out, int64_t M, int64_t N, int64_t ldo, bool f32, CUtensorMap* map) {
+  EncodeTiledFn enc = nullptr;
+  if (int rc = encode_tiled_fn(&enc)) return rc;
+  const int esz = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {cuuint64_t(N), cuuint64_t(M)};
+  cuuint64_t strides[1] = {cuuint64_t(ldo) * esz};
+  cuuint32_t box[2] = {cuuint32_t(128 / esz), 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrInvalid;
+}
+
+constexpr int kTileChoices[] = {64, 96, 128, 160, 192, 256};
 
 }  // namespace
 
-int gemm_pick_bn(int64_t M, int64_t N, int64_t K, int sms) {
-  // Cost model: waves of persistent tiles x per-tile time, where a tile's main loop is bounded by the larger of
-  // the tensor-core time (2*BN clocks per 64-deep K block at 8192 FLOP/clk/SM) and the time to stream its
-  // operands into shared memory (~64 B/clk/SM), plus a fixed epilogue/turnaround cost per tile.
+namespace {
+// Split-K tile counters live in a fixed region at the start of the workspace (split-K only runs when the tiles
+// number at most half the SMs), so a workspace reused across problems always finds them at the same place.
+constexpr size_t kSplitCounterBytes = 4096;
+
+// Modelled time (SM clocks) of a plan: waves of persistent work units x per-unit time. A unit's main loop is
+// bounded by the larger of the tensor-core time (2*BN clocks per 64-deep K block at 8192 FLOP/clk/SM) and the
+// time to stream its operands into shared memory (~64 B/clk/SM); each unit pays a fixed pipeline fill, and a
+// split tile pays for writing and re-reading its f32 partials.
+double plan_cost(int64_t M, int64_t N, int64_t kb, int bn, int splits, int sms) {
+  const int64_t tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + bn - 1) / bn);
+  const int64_t units = tiles * splits;
+  const int64_t waves = (units + sms - 1) / sms;
+  const int64_t kb_unit = (kb + splits - 1) / splits;
+  const double mma = 2.0 * bn;
+  const double load = (kGemmBM + bn) * 128.0 / 64.0;
+  double t = double(kb_unit) * std::max(mma, load) + 1500.0 + 8.0 * bn;
+  if (splits > 1) t += 8.0 * bn + 8.0 * bn * (splits - 1) + 1000.0;
+  return double(waves) * t;
+}
+}  // namespace
+
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant) {
   const int64_t kb = (K + kGemmBK - 1) / kGemmBK;
-  const int64_t mblk = (M + kGemmBM - 1) / kGemmBM;
-  double best = 1e300;
-  int best_bn = 128;
+  GemmPlan best{128, 1, int(kb), 0};
+  double best_cost = 1e300;
   for (int bn : kTileChoices) {
-    const int64_t tiles = mblk * ((N + bn - 1) / bn);
-    const int64_t waves = (tiles + sms - 1) / sms;
-    const double mma = 2.0 * bn;
-    const double load = (kGemmBM + bn) * 128.0 / 64.0;
-    const double t_tile = double(kb) * std::max(mma, load) + 150.0 + 4.0 * bn;
-    const double cost = double(waves) * t_tile;
-    if (cost < best * 0.999 || (cost <= best * 1.001 && bn > best_bn)) {
-      best = cost;
-      best_bn = bn;
+    if (variant && bn != variant) continue;
+    const int64_t tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + bn - 1) / bn);
+    // Split K only when the tiles leave most SMs idle and each split keeps >= 4 K blocks.
+    int max_split = 1;
+    if (tiles * 2 <= sms && tiles * 4 <= int64_t(kSplitCounterBytes) && kb >= 8) max_split = int(std::min<int64_t>(std::min<int64_t>(sms / tiles, kb / 4), 16));
+    for (int sp = 1; sp <= max_split; ++sp) {
+      const int kps = int((kb + sp - 1) / sp);
+      const int eff = int((kb + kps - 1) / kps);  // splits actually needed with kps blocks each
+      if (eff != sp) continue;
+      const double cost = plan_cost(M, N, kb, bn, sp, sms);
+      if (cost < best_cost * 0.999 || (cost <= best_cost * 1.001 && bn > best.bn && sp <= best.splits)) {
+        best_cost = cost;
+        best.bn = bn;
+        best.splits = sp;
+        best.kb_per_split = kps;
+        best.split_ws_bytes = sp > 1 ? kSplitCounterBytes + size_t(tiles) * sp * bn * kGemmBM * 4 : 0;
+      }
     }
   }
-  return best_bn;
+  return best;
 }
 
 int gemm_encode_b_map(const void* w, int64_t ldw, int64_t N, int64_t K, int bn, CUtensorMap* out) {
@@ -348,10 +549,18 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
                                                     (long long)p.M, (long long)p.N, (long long)p.K);
   if (p.M > INT32_MAX / 2 || p.N > INT32_MAX / 2 || p.K > INT32_MAX / 2)
     return fail(kErrInvalid, "GEMM dimension too large");
-  int bn = p.variant ? p.variant : gemm_pick_bn(p.M, p.N, p.K, dev->sms);
-  bool known = false;
-  for (int c : kTileChoices) known |= (c == bn);
-  if (!known) return fail(kErrUnsupported, "no GEMM variant with an N tile of %d", bn);
+  if (p.variant) {
+    bool known = false;
+    for (int c : kTileChoices) known |= (c == p.variant);
+    if (!known) return fail(kErrUnsupported, "no GEMM variant with an N tile of %d", p.variant);
+  }
+  GemmPlan plan = gemm_plan(p.M, p.N, p.K, dev->sms, p.variant);
+  const int bn = plan.bn;
+  if (plan.splits > 1 && (p.ws_split == nullptr || p.ws_split_bytes < plan.split_ws_bytes ||
+                          (reinterpret_cast<uintptr_t>(p.ws_split) & 255) != 0)) {
+    plan.splits = 1;  // no room for partials: one CTA per tile over all of K
+    plan.kb_per_split = int((p.K + kGemmBK - 1) / kGemmBK);
+  }
 
   CUtensorMap mx, mw;
   if (int rc = encode_kmajor_map(p.x, p.M, p.K, p.ldx, kGemmBM, &mx)) return rc;
@@ -361,7 +570,15 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
     return rc;
   }
 
+  // TMA-store epilogue when the output rows are 16-byte aligned; otherwise direct predicated stores.
+  CUtensorMap mo;
+  memset(&mo, 0, sizeof(mo));
+  const int esz = p.out_f32 ? 4 : 2;
+  bool tma_store = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && (p.ldo * esz) % 16 == 0;
+  if (tma_store && encode_out_map(p.out, p.M, p.N, p.ldo, p.out_f32 != 0, &mo) != kOk) tma_store = false;
+
   GemmArgs a;
+  a.tma_store = tma_store ? 1 : 0;
   a.M = int(p.M);
   a.N = int(p.N);
   a.K = int(p.K);
@@ -376,17 +593,23 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.out = p.out;
   a.ldo = p.ldo;
   a.out_f32 = p.out_f32;
+  a.splits = plan.splits;
+  a.kb_per_split = plan.kb_per_split;
+  a.ws_counter = plan.splits > 1 ? static_cast<unsigned int*>(p.ws_split) : nullptr;
+  a.ws_partial =
+      plan.splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(p.ws_split) + kSplitCounterBytes) : nullptr;
   a.ctl.status = dev->status;
   a.ctl.timeout_ns = wait_timeout_ns();
   a.ctl.debug = p.debug;
-  const int grid = int(std::min<int64_t>(tiles, dev->sms));
+  const int grid = int(std::min<int64_t>(tiles * plan.splits, dev->sms));
 
   switch (bn) {
-    case 64: return launch_variant<64, 8>(mx, mw, a, grid, stream, dev->device);
-    case 80: return launch_variant<80, 8>(mx, mw, a, grid, stream, dev->device);
-    case 128: return launch_variant<128, 6>(mx, mw, a, grid, stream, dev->device);
-    case 160: return launch_variant<160, 5>(mx, mw, a, grid, stream, dev->device);
-    case 256: return launch_variant<256, 4>(mx, mw, a, grid, stream, dev->device);
+    case 64: return launch_variant<64, 8>(mx, mw, mo, a, grid, stream, dev->device);
+    case 96: return launch_variant<96, 6>(mx, mw, mo, a, grid, stream, dev->device);
+    case 128: return launch_variant<128, 6>(mx, mw, mo, a, grid, stream, dev->device);
+    case 160: return launch_variant<160, 5>(mx, mw, mo, a, grid, stream, dev->device);
+    case 192: return launch_variant<192, 4>(mx, mw, mo, a, grid, stream, dev->device);
+    case 256: return launch_variant<256, 4>(mx, mw, mo, a, grid, stream, dev->device);
   }
   return fail(kErrUnsupported, "no GEMM variant with an N tile of %d", bn);
 }

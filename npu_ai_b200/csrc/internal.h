@@ -53,12 +53,20 @@ struct GemmProblem {
   int64_t ldo;
   int out_f32;       // 1: f32 output, 0: bf16
   int64_t M, N, K;
-  int variant;       // 0 = automatic, else a forced N tile (64, 80, 128, 160, 256)
+  int variant;       // 0 = automatic, else a forced N tile (64, 96, 128, 160, 192, 256)
   const CUtensorMap* w_map_cache;  // optional cached B tensor map (matching the chosen tile), may be null
+  void* ws_split;                  // split-K workspace: zeroed counters, then f32 partials (may be null)
+  size_t ws_split_bytes;
   uint32_t debug;
 };
-// Chooses the N tile for a problem (what `variant == 0` resolves to).
-int gemm_pick_bn(int64_t M, int64_t N, int64_t K, int sms);
+// Launch plan for a problem: the N tile and the split-K factor (what `variant == 0` resolves to).
+struct GemmPlan {
+  int bn;
+  int splits;
+  int kb_per_split;
+  size_t split_ws_bytes;  // bytes of split-K workspace the plan needs (0 when splits == 1)
+};
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant);
 int gemm_encode_b_map(const void* w, int64_t ldw, int64_t N, int64_t K, int bn, CUtensorMap* out);
 int gemm_launch(const GemmProblem& p, cudaStream_t stream);
 // bf16 copy of a row-strided matrix into a dense [rows, cols_pad] buffer, zero-filling the pad columns.

@@ -52,6 +52,15 @@ __device__ __forceinline__ bool elect_one() {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with the programmatic-serialization attribute may start while
+// the previous kernel on the stream is still running; it must wait before touching memory that kernel writes.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -83,12 +92,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait until the phase with the given parity of `bar` has completed. Gives up (returns false) when the
-// deadline passes or when *abort is set by another role of the CTA; on a deadline it raises the CTA's
-// abort flag and ORs `code` into the status word.
-static __device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                               const KernelCtl& ctl, uint32_t code) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Slow path of mbar_wait_bounded (out of line: the fast path is one inlined try_wait).
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                   const KernelCtl& ctl, uint32_t code) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -101,6 +107,15 @@ static __device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t pa
       }
     }
   }
+}
+
+// Wait until the phase with the given parity of `bar` has completed. Gives up (returns false) when the
+// deadline passes or when *abort is set by another role of the CTA; on a deadline it raises the CTA's
+// abort flag and ORs `code` into the status word.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                  const KernelCtl& ctl, uint32_t code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort, ctl, code);
 }
 
 // Bounded wait used only while draining after an abort: no abort check, a fixed generous deadline.
@@ -138,6 +153,26 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
       "[%2];" ::"r"(smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+
+// TMA tile store shared -> global (out-of-bounds rows/columns of the box are not written).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups of this thread are still reading shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until all committed bulk groups of this thread have completed (writes visible).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Named barrier over `count` threads (a multiple of 32) of the CTA; id 0 is __syncthreads'.
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // Make generic-proxy writes to shared memory (st.shared) visible to the async proxy (tensor core, TMA).
@@ -243,6 +278,12 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
 // K-major operand staged by a 128-byte-swizzled TMA box (rows of 64 bf16 = 128 B, 8-row atoms of 1 KB).
 __device__ __forceinline__ uint64_t smem_desc_kmajor_sw128(uint32_t saddr) {
   return smem_desc(saddr, 16, 1024, 2);
+}
+
+// MN-major operand in 128-byte-swizzled atoms (64 MN elements x 8 K rows of 128 B per 1 KB block): `lbo_bytes` is
+// the distance between consecutive 64-element MN atoms, K groups of 8 rows are 1 KB apart.
+__device__ __forceinline__ uint64_t smem_desc_mnmajor_sw128(uint32_t saddr, uint32_t lbo_bytes) {
+  return smem_desc(saddr, lbo_bytes, 1024, 2);
 }
 
 // Operand in the canonical no-swizzle ("interleaved") layout: 8 x 16 B core matrices of 128 contiguous bytes.

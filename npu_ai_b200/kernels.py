@@ -42,18 +42,45 @@ def register_weight(w_nk: torch.Tensor) -> int:
     return h.value
 
 
+def gemm_plan(M: int, N: int, K: int, variant: int = 0, device: torch.device | int | None = None) -> tuple[int, int]:
+    """(N tile, split-K factor) the library picks for an M x K x N GEMM on the device."""
+    bn, sp = ctypes.c_int(0), ctypes.c_int(0)
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        _lib.call("npub200_gemm_plan", int(M), int(N), int(K), int(variant), ctypes.byref(bn), ctypes.byref(sp))
+    return bn.value, sp.value
+
+
 def release_weight(handle: int) -> None:
     _lib.call("npub200_weight_release", handle)
 
 
-def _gemm_workspace(x: torch.Tensor, w: torch.Tensor | None, M: int, K: int, N: int) -> torch.Tensor | None:
+# One persistent workspace per (device, stream): its leading split-K counters must be zero the first time it is
+# used and the kernels leave them zero, so it is allocated zeroed once and only ever grown (never handed back to the
+# caching allocator while this process may still launch on that stream).
+_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _gemm_workspace(x: torch.Tensor, w: torch.Tensor | None, M: int, K: int, N: int, variant: int):
     nbytes = ctypes.c_size_t(0)
     _lib.call("npub200_gemm_workspace_size", ctypes.c_void_p(x.data_ptr()), x.stride(0), M, K,
               ctypes.c_void_p(w.data_ptr()) if w is not None else None, w.stride(0) if w is not None else 0, N,
-              ctypes.byref(nbytes))
+              int(variant), ctypes.byref(nbytes))
     if nbytes.value == 0:
         return None
-    return torch.empty(nbytes.value, dtype=torch.uint8, device=x.device)
+    key = (x.device.index or 0, torch.cuda.current_stream(x.device).cuda_stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes.value:
+        size = max(nbytes.value, 1 << 22)
+        size = 1 << (size - 1).bit_length()
+        ws = torch.zeros(size, dtype=torch.uint8, device=x.device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def reset_workspaces() -> None:
+    """Re-zero the cached workspaces (after a kernel aborted, its split-K counters may be left non-zero)."""
+    for ws in _WORKSPACES.values():
+        ws.zero_()
 
 
 def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
@@ -79,7 +106,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out
     if bias is not None:
         if bias.dtype not in _DT or bias.numel() != N or not bias.is_contiguous():
             raise ValueError("bias must be a contiguous [N] bf16/f32 vector")
-    ws = _gemm_workspace(x, None if handle is not None else w, M, K, N)
+    ws = _gemm_workspace(x, None if handle is not None else w, M, K, N, variant)
     args_tail = (ctypes.c_void_p(bias.data_ptr()) if bias is not None else None,
                  _DT[bias.dtype] if bias is not None else _lib.DTYPE_BF16,
                  ctypes.c_void_p(out.data_ptr()), out.stride(0), _DT[out.dtype],
@@ -161,6 +188,7 @@ def check_status(device: torch.device | int | None = None) -> None:
     """Raise RuntimeError if a kernel reported a failure (the reference's NpuProgram.wait, xdna1_program.py:475-479)."""
     bits = status(device)
     if bits:
+        reset_workspaces()
         raise RuntimeError(f"GPU kernel reported failure status 0x{bits:x} (a bounded wait expired)")
 
 

@@ -41,13 +41,15 @@ def _check(o, ref, tol=TOL_ABS):
 @pytest.mark.parametrize("shape", [(2, 8, 4096, 4096, 40), (2, 8, 1024, 1024, 80), (2, 8, 256, 256, 160),
                                    (2, 8, 4096, 77, 40)],
                          ids=["self64x64_d40", "self32x32_d80", "self16x16_d160", "cross4096x77_d40"])
-def test_baseline_blocks(cuda_device, shape):
-    """the SD1.5 self-/cross-attention blocks, all (b, h) pairs in one launch."""
+@pytest.mark.parametrize("variant", [0, 64, 128])
+def test_baseline_blocks(cuda_device, shape, variant):
+    """the SD1.5 self-/cross-attention blocks, all (b, h) pairs in one launch, for the default
+    and both key-tile variants (64 keys: two CTAs per SM; 128 keys: one)."""
     B, H, Sq, Skv, D = shape
     q, k, v = _qkv(B, H, Sq, Skv, D, seed=D)
     ref = attention_ref(q, k, v, H)
-    _check(_run(q, k, v, H), ref)
-    _check(_run(q, k, v, H, out_dtype=torch.bfloat16), ref)
+    _check(_run(q, k, v, H, variant=variant), ref)
+    _check(_run(q, k, v, H, out_dtype=torch.bfloat16, variant=variant), ref)
 
 
 @pytest.mark.parametrize("shape", ["1x4x256x256x40", "1x4x512x256x80", "2x8x1024x1024x80"])
