@@ -80,6 +80,22 @@ int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t wei
                    int variant, void* stream);
 
 /* ----------------------------------------------------------------------------------------------------------
+ * GEMM without a workspace, for callers that cannot allocate device memory (a host whose device memory is owned
+ * by its own pool manager and may not grow during a request, an FFI binding holding only the pointers it was
+ * given, code that must not call cudaMalloc because it synchronises the device). No counterpart in the reference:
+ * its NPU runner allocates its own pinned buffers. Same arguments and result as npub200_gemm minus the
+ * workspace; the scratch is one fixed device array of NPUB200_NOALLOC_SCRATCH_BYTES per GPU, held from library
+ * load to process exit, and this call allocates nothing. A shape whose scratch need exceeds the array is rejected
+ * with NPUB200_EINVAL. The first call on a device resolves the array and clears its counters (make it before any
+ * stream capture). All calls share the array and it keeps the last call's contents: calls that overlap on the GPU
+ * (several streams, several host threads) race and must be serialised by the caller, e.g. on one stream.
+ * ---------------------------------------------------------------------------------------------------------- */
+#define NPUB200_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+int npub200_gemm_noalloc(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                         const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype, int variant,
+                         void* stream);
+
+/* ----------------------------------------------------------------------------------------------------------
  * Fused attention: out = softmax(Q K^T * scale) V for every (batch, head) pair in ONE launch; bf16 q/k/v,
  * f32 softmax statistics and accumulation, out bf16 or f32. Replaces NpuGemm.attention / _attention_fused
  * (npu/xdna1_gemm.py:499-752), NpuProgram.submit_attn (npu/xdna1_program.py:461-473) and the AIE flash kernel

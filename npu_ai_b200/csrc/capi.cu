@@ -155,9 +155,19 @@ int check_gemm_common(int64_t m, int64_t k, int64_t n, int bias_dtype, const voi
   return kOk;
 }
 
-int gemm_common(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
-                const CUtensorMap* w_map, const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
-                void* workspace, size_t workspace_bytes, int variant, void* stream) {
+}  // namespace
+
+namespace npub200 {
+
+size_t gemm_workspace_bytes(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                            int variant, int sms) {
+  return gemm_ws_layout(x, ldx, m, k, w, ldw, n, variant, sms).total;
+}
+
+int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                        const CUtensorMap* w_map, const void* bias, int bias_dtype, void* out, int64_t ldo,
+                        int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream) {
+  if (int rc = check_gemm_common(m, k, n, bias_dtype, out, ldo, out_dtype)) return rc;
   if (x == nullptr || w == nullptr) return fail(kErrInvalid, "GEMM operand pointer is null");
   if (ldx < k) return fail(kErrInvalid, "x row stride %lld < K=%lld", (long long)ldx, (long long)k);
   if (ldw < k) return fail(kErrInvalid, "W row stride %lld < K=%lld", (long long)ldw, (long long)k);
@@ -213,6 +223,17 @@ int gemm_common(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w,
     p.ws_split_bytes = L.split_bytes;
   }
   return gemm_launch(p, st);
+}
+
+}  // namespace npub200
+
+namespace {
+
+int gemm_common(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                const CUtensorMap* w_map, const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
+                void* workspace, size_t workspace_bytes, int variant, void* stream) {
+  return gemm_with_workspace(x, ldx, m, k, w, ldw, n, w_map, bias, bias_dtype, out, ldo, out_dtype, workspace,
+                             workspace_bytes, variant, stream);
 }
 
 }  // namespace
@@ -375,6 +396,8 @@ int npub200_status_read(void* stream, uint32_t* bits_out, int clear) {
   if (clear && bits) {
     const uint32_t zero = 0;
     if (int rc = check_cuda(cudaMemcpyToSymbol(g_status_word, &zero, sizeof(zero)), "clear status word")) return rc;
+    if (int rc = noalloc_reset_counters(d->device, st)) return rc;
+    if (int rc = check_cuda(cudaStreamSynchronize(st), "cudaStreamSynchronize")) return rc;
   }
   if (bits_out) *bits_out = bits;
   return kOk;

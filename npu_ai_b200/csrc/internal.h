@@ -68,10 +68,20 @@ struct GemmPlan {
 };
 GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant);
 int gemm_encode_b_map(const void* w, int64_t ldw, int64_t N, int64_t K, int bn, CUtensorMap* out);
+// Bytes of workspace the GEMM entry points use for a problem (split-K counters + partials, repack buffers).
+size_t gemm_workspace_bytes(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                            int variant, int sms);
+// The GEMM entry point's body with a caller-given workspace (argument checks, repacking, split-K, launch).
+int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                        const CUtensorMap* w_map, const void* bias, int bias_dtype, void* out, int64_t ldo,
+                        int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream);
 int gemm_launch(const GemmProblem& p, cudaStream_t stream);
 // bf16 copy of a row-strided matrix into a dense [rows, cols_pad] buffer, zero-filling the pad columns.
 int repack_rows_bf16(const void* src, int64_t ld_src, int64_t rows, int64_t cols, void* dst, int64_t cols_pad,
                      cudaStream_t stream);
+
+// Clears the no-allocation entry point's split-K counters on `device` (after a kernel reported a failure).
+int noalloc_reset_counters(int device, cudaStream_t stream);
 
 // ---- attention ---------------------------------------------------------------------------------------------------
 struct AttnProblem {
