@@ -510,6 +510,121 @@ def run_e2e(args, dist, device, total_flops) -> dict:
             "ms_per_step": round(e2e_ms, 3), "api": "npu_ai_b200.runner.NpuGemm.linear / .attention"}
 
 
+# ----------------------------------------------------------------------------------------------------------------
+# UNet workload: SD1.5-architecture UNet denoise steps (BASELINE configs 3 and 4)
+# ----------------------------------------------------------------------------------------------------------------
+def run_unet(args, dist) -> None:
+    """Euler CFG denoise steps of a random-init SD1.5-architecture UNet with every Linear and attention on the B200
+    kernels (through the ComfyUI node runtime). The batch (prompts x CFG pair) is sharded over the ranks with each
+    prompt's pair local; latents are all-gathered over NCCL every step. One step = one UNet call on the whole batch
+    plus the guidance combine and the Euler update, captured as a CUDA graph. Strong scaling: the total batch is
+    fixed as GPUs are added."""
+    from npu_ai_b200 import comfy_nodes as cn
+    from npu_ai_b200 import kernels
+    from npu_ai_b200.sd15_unet import build_unet, karras_sigmas, prompt_shard, seeded_prompts, sigma_to_t
+    device = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(device)
+    P = args.batch // 2
+    lo, hi = prompt_shard(P, dist.world, dist.rank)
+    if hi - lo < 1:
+        raise SystemExit("need at least one prompt (two images: uncond + cond) per rank")
+    model = build_unet(seed=0, device=device, dtype=torch.bfloat16)
+    rt = cn._get_runtime(device)
+    rt.min_tokens = 64
+    rt.take_over(model, 320, ("time_embed", "label_emb", "emb_layers"))
+    rt.attn.mode = "gpu"
+    rt.attn.min_tokens = 64
+    rt.enabled = True
+    to = {"optimized_attention_override": cn._gpu_attention_override}
+    lat, ctx, unc = seeded_prompts(P, args.latent, seed=1, device=device, dtype=torch.bfloat16)
+    lat, ctx, unc = lat[lo:hi].contiguous(), ctx[lo:hi].contiguous(), unc[lo:hi].contiguous()
+    cond = torch.cat([unc, ctx])
+    sigmas = karras_sigmas(args.unet_steps).to(device)
+    sig = torch.zeros(2, device=device)  # [sigma, sigma_next] of the step being replayed
+    x = (lat.float() * sigmas[0]).contiguous()
+    full = torch.empty((P, *lat.shape[1:]), dtype=torch.float32, device=device) if dist.world > 1 else None
+
+    def step():
+        s, s_next = sig[0], sig[1]
+        x_in = (torch.cat([x, x]) / torch.sqrt(s * s + 1.0)).to(torch.bfloat16)
+        t = sigma_to_t(s).expand(x_in.shape[0])
+        eps = model(x_in, t, cond, to).float()
+        eu, ec = eps.chunk(2)
+        x.add_((s_next - s) * (eu + 7.5 * (ec - eu)))
+        if full is not None:
+            dist.pg.all_gather_into_tensor(full, x)
+
+    def set_step(i):
+        i %= args.unet_steps
+        sig.copy_(torch.stack([sigmas[i], sigmas[i + 1]]))
+
+    with torch.no_grad():
+        for i in range(max(3, args.warmup)):
+            set_step(i)
+            step()
+        torch.cuda.synchronize()
+        cs = torch.cuda.Stream(device)
+        cs.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(cs):
+            step()
+        torch.cuda.current_stream(device).wait_stream(cs)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cs):
+            step()
+        torch.cuda.synchronize()
+        kernels.check_status(device)
+        dist.barrier()
+        sampler = ClockSampler([_gpu_uuid(dist.local_rank)]) if dist.rank == 0 else None
+        if sampler is not None:
+            sampler.start()
+            time.sleep(0.3)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        if sampler is not None:
+            sampler.mark(True)
+        t0.record()
+        for i in range(args.steps):
+            set_step(i)
+            g.replay()
+        t1.record()
+        torch.cuda.synchronize()
+        if sampler is not None:
+            sampler.mark(False)
+        dist.barrier()
+        clocks = sampler.stop() if sampler is not None else None
+        kernels.check_status(device)
+    ms = dist.max(t0.elapsed_time(t1) / args.steps, device)
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        torch.set_num_threads(os.cpu_count() or 1)
+        cpu_model = build_unet(seed=0, device="cpu", dtype=torch.bfloat16).float()
+        xc = torch.cat([lat, lat]).float().cpu()
+        tc = torch.full((xc.shape[0],), 500.0)
+        with torch.no_grad():
+            cpu_model(xc[:, :, :8, :8], tc, cond.float().cpu())
+            c0 = time.perf_counter()
+            cpu_model(xc, tc, cond.float().cpu())
+            cdt = time.perf_counter() - c0
+        cpu = {"value": round(1.0 / cdt, 4), "unit": "steps/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"one UNet call (batch {xc.shape[0]}, {args.latent}x{args.latent} latent) in f32 on the "
+                         f"host with torch's CPU F.linear/SDPA (the reference's CPU fallback): {cdt:.2f} s"}
+    if dist.rank == 0:
+        line = {"metric": "SD1.5 UNet denoise steps/s", "value": round(1e3 / ms, 3), "unit": "steps/s",
+                "n_gpus": dist.world, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 3),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic",
+                "config": {"workload": f"sd15-unet-random-init batch {args.batch} ({P} prompts x CFG) "
+                                       f"{args.latent}x{args.latent} latent, {args.unet_steps} Euler steps per image",
+                           "parallelism": f"batch-sharded x{dist.world}, latents all-gathered per step",
+                           "s_per_image": round(ms * args.unet_steps / 1e3 / P, 5),
+                           "linear_layers_on_gemm_kernel": len(rt.weights)},
+                "execution": "CUDA graph of one denoise step",
+                "cpu_baseline": cpu, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    del g
+
+
 def run_case(args) -> None:
     """--case: one kernel on one shape, `warmup` + `steps` launches (the small cases the ncu captures use)."""
     from npu_ai_b200 import kernels
@@ -552,6 +667,11 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--case", default=None, help="time one kernel: gemm:M,K,N or attn:B,H,Sq,Skv,D")
+    ap.add_argument("--workload", choices=["hotpath", "unet"], default="hotpath",
+                    help="hotpath: the GEMM sweep + attention blocks (default); unet: SD1.5 UNet denoise steps")
+    ap.add_argument("--batch", type=int, default=2, help="unet: images per step, both CFG halves (2 = 1 prompt)")
+    ap.add_argument("--latent", type=int, default=64, help="unet: latent height/width")
+    ap.add_argument("--unet-steps", type=int, default=4, help="unet: Euler steps per image")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     if args.case:
@@ -564,7 +684,10 @@ def main(argv=None) -> int:
         return 0
     dist = Dist(use_cuda=True)
     try:
-        run_ours(args, dist)
+        if args.workload == "unet":
+            run_unet(args, dist)
+        else:
+            run_ours(args, dist)
     finally:
         dist.close()
     return 0

@@ -112,7 +112,10 @@ bool tma_rows_ok(const void* p, int64_t ld, int64_t cols) { return aligned16(p) 
 
 int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
-// Workspace layout: [split-K region: zeroed tile counters + f32 partials][repacked x][repacked W].
+// Workspace layout: [4 KiB split-K tile counters][f32 split-K partials][repacked x][repacked W]. The counter
+// region is reserved whenever a workspace is used at all, so a call that only repacks never writes over the
+// counters a later split-K call on the same workspace relies on being zero.
+constexpr size_t kCounterRegion = 4096;
 struct WsLayout {
   size_t split_bytes = 0;
   size_t x_off = 0, x_bytes = 0;
@@ -125,8 +128,8 @@ WsLayout gemm_ws_layout(const void* x, int64_t ldx, int64_t m, int64_t k, const 
   WsLayout L;
   const int64_t kp = round_up(k, 8);
   const bool pad_k = (k % 8) != 0;
-  L.split_bytes = sms > 0 ? gemm_plan(m, n, kp, sms, variant).split_ws_bytes : 0;
-  size_t off = L.split_bytes;
+  L.split_bytes = sms > 0 ? gemm_plan(m, n, kp, sms, variant).split_ws_bytes : 0;  // counters + partials
+  size_t off = L.split_bytes > 0 ? L.split_bytes : kCounterRegion;
   if (pad_k || !tma_rows_ok(x, ldx, k)) {
     L.x_off = off;
     L.x_bytes = size_t(round_up(m * kp * 2, 256));
@@ -137,7 +140,7 @@ WsLayout gemm_ws_layout(const void* x, int64_t ldx, int64_t m, int64_t k, const 
     L.w_bytes = size_t(round_up(n * kp * 2, 256));
     off += L.w_bytes;
   }
-  L.total = off;
+  L.total = (L.split_bytes > 0 || L.x_bytes > 0 || L.w_bytes > 0) ? off : 0;
   return L;
 }
 

@@ -252,3 +252,50 @@ def euler_cfg_sample(model, latent, context, uncond, steps: int = 4, cfg: float 
         if step_callback is not None:
             step_callback(i, x)
     return x
+
+
+def prompt_shard(n_prompts: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous prompt range [lo, hi) of `rank`: prompts split as evenly as possible, each prompt's CFG pair
+    (uncond, cond) stays on one rank so the guidance combine and the Euler update need no communication."""
+    base, extra = divmod(n_prompts, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def seeded_prompts(n_prompts: int, latent_hw: int, seed: int = 0, device="cpu", dtype=torch.float32,
+                   context_len: int = 77, context_dim: int = 768):
+    """Per-prompt seeded latents [P,4,h,w] ~ N(0,1), text contexts and unconditional contexts [P,77,768] ~ N(0,1).
+    Each prompt draws from its own generator, so a prompt's inputs do not depend on how prompts are sharded."""
+    lat, ctx, unc = [], [], []
+    for p in range(n_prompts):
+        g = torch.Generator().manual_seed(seed * 100003 + p)
+        lat.append(torch.randn(1, 4, latent_hw, latent_hw, generator=g))
+        ctx.append(torch.randn(1, context_len, context_dim, generator=g))
+        unc.append(torch.randn(1, context_len, context_dim, generator=g))
+    cat = lambda xs: torch.cat(xs).to(device=device, dtype=dtype)  # noqa: E731
+    return cat(lat), cat(ctx), cat(unc)
+
+
+def sample_sharded(model, latents, context, uncond, steps: int = 4, cfg: float = 7.5, transformer_options=None,
+                   group=None):
+    """Euler CFG sampling of all prompts with the batch sharded over the ranks of `group` (torch.distributed):
+    each rank denoises its own prompts (both CFG halves) and the final latents are all-gathered. `latents`,
+    `context`, `uncond` hold ALL prompts; every rank returns the full result. Without a process group it is plain
+    single-device sampling."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group) if (group is not None or (dist.is_available() and dist.is_initialized())) else 1
+    rank = dist.get_rank(group) if world > 1 else 0
+    P = latents.shape[0]
+    lo, hi = prompt_shard(P, world, rank)
+    mine = euler_cfg_sample(model, latents[lo:hi], context[lo:hi], uncond[lo:hi], steps=steps, cfg=cfg,
+                            transformer_options=transformer_options)
+    if world == 1:
+        return mine
+    # Uneven shards are padded to the largest one for a single all-gather, then trimmed.
+    width = -(-P // world)
+    padded = torch.zeros((width, *latents.shape[1:]), dtype=mine.dtype, device=mine.device)
+    padded[: hi - lo] = mine
+    gathered = torch.empty((world * width, *latents.shape[1:]), dtype=mine.dtype, device=mine.device)
+    dist.all_gather_into_tensor(gathered, padded, group=group)
+    return torch.cat([gathered[r * width: r * width + (prompt_shard(P, world, r)[1] - prompt_shard(P, world, r)[0])]
+                      for r in range(world)])

@@ -177,3 +177,11 @@ def test_split_k_deterministic_and_reused_workspace(cuda_device, MKN):
     _check_f32(_run(x2, w2, b2), linear_ref(x2, w2, b2))
     y2 = _run(x, w, b)
     assert torch.equal(y1, y2), "split-K result changed between identical calls"
+
+
+def test_repack_then_split_k_share_workspace(cuda_device):
+    """A call that only repacks (K % 8 != 0) followed by split-K calls on the same cached workspace: the repack must
+    not land on the split-K counters."""
+    for MKN in [(100, 100, 100), (154, 768, 320), (99, 1001, 77), (512, 1280, 1280), (77, 5120, 1280)]:
+        x, w, b = _inputs(*MKN, seed=sum(MKN))
+        _check_f32(_run(x, w, b), linear_ref(x, w, b))
