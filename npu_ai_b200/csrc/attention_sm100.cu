@@ -579,9 +579,10 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   for (const void* ptr : {p.q, p.k, p.v})
     if (reinterpret_cast<uintptr_t>(ptr) & 15u) return fail(kErrInvalid, "q/k/v base addresses must be 16-byte aligned");
   const int64_t DP = (p.D + 15) / 16 * 16;
-  // Key tile (variant): 128 keys per tile by default; 64 keys halves the per-CTA footprint (two CTAs share an SM
-  // when it fits) and is the only tile for head dims above 128.
-  int BN = p.variant ? p.variant : 128;
+  // Key tile (variant): for head dims up to 64 the default is 64 keys, which halves the per-CTA footprint so two
+  // CTAs share an SM (their softmax warps hide each other's latencies); 128 keys otherwise. 64 is the only tile for
+  // head dims above 128.
+  int BN = p.variant ? p.variant : (DP <= 64 ? 64 : 128);
   if (BN != 64 && BN != 128) return fail(kErrUnsupported, "attention key tile %d (variants: 64, 128)", BN);
   if (DP > 128) BN = 64;
 

@@ -27,7 +27,8 @@ constexpr int kGemmThreads = 192;
 
 struct GemmArgs {
   int M, N, K;
-  int num_m_blk, num_tiles, num_kb;
+  int num_m_blk, num_n_blk, num_tiles, num_kb;
+  int n_fastest;  // tile raster: 1 = N tiles innermost (x stays in L2 across them), 0 = M tiles innermost
   const void* bias;
   int bias_f32;
   void* out;
@@ -140,6 +141,16 @@ __device__ __forceinline__ void store_row32_direct(const GemmArgs& a, int grow, 
   }
 }
 
+__device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& m_blk, int& n_blk) {
+  if (a.n_fastest) {
+    m_blk = tile / a.num_n_blk;
+    n_blk = tile - m_blk * a.num_n_blk;
+  } else {
+    n_blk = tile / a.num_m_blk;
+    m_blk = tile - n_blk * a.num_m_blk;
+  }
+}
+
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
@@ -200,21 +211,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
+      // The weight never depends on the previous kernel on the stream: the first stages' W tiles are requested
+      // before waiting on it (programmatic dependent launch), so their fetch overlaps that kernel's tail.
+      int pre = 0;
+      if (int(blockIdx.x) < num_units) {
+        int mb, nb;
+        tile_coords(args, int(blockIdx.x) / args.splits, mb, nb);
+        const int kb0 = (int(blockIdx.x) % args.splits) * args.kb_per_split;
+        pre = min(STAGES, min(num_kb, kb0 + args.kb_per_split) - kb0);
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], L::kStageBytes);
+          tma_load_2d(&tm_w, &full[i], sB + i * L::kBBytes, (kb0 + i) * kGemmBK, nb * BN);
+        }
+      }
       pdl_wait();  // x may be the previous kernel's output
       for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
         const int tile = unit / args.splits;
-        const int m0 = (tile % num_m) * kGemmBM;
-        const int n0 = (tile / num_m) * BN;
+        int mb, nb;
+        tile_coords(args, tile, mb, nb);
+        const int m0 = mb * kGemmBM;
+        const int n0 = nb * BN;
         const int kb_begin = (unit % args.splits) * args.kb_per_split;
         const int kb_end = min(num_kb, kb_begin + args.kb_per_split);
         for (int kb = kb_begin; kb < kb_end; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutProducer)) {
-            ok = false;
-            break;
+          if (pre > 0) {
+            // stage already armed and its W tile in flight (first stages of the first unit)
+            tma_load_2d(&tm_x, &full[stage], sA + stage * L::kABytes, kb * kGemmBK, m0);
+            --pre;
+          } else {
+            if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+            tma_load_2d(&tm_x, &full[stage], sA + stage * L::kABytes, kb * kGemmBK, m0);
+            tma_load_2d(&tm_w, &full[stage], sB + stage * L::kBBytes, kb * kGemmBK, n0);
           }
-          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-          tma_load_2d(&tm_x, &full[stage], sA + stage * L::kABytes, kb * kGemmBK, m0);
-          tma_load_2d(&tm_w, &full[stage], sB + stage * L::kBBytes, kb * kGemmBK, n0);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -305,12 +337,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      if (args.bias != nullptr && warp == 2) {
+        // Pull this tile's bias into L2 while the main loop runs (one 128-byte line per lane).
+        int pmb, pnb;
+        tile_coords(args, unit / splits, pmb, pnb);
+        const int esz = args.bias_f32 ? 4 : 2;
+        const int bytes = min(BN, args.N - pnb * BN) * esz;
+        if (lane * 128 < bytes)
+          prefetch_l2(static_cast<const uint8_t*>(args.bias) + size_t(pnb) * BN * esz + lane * 128);
+      }
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.ctl, kStatusTimeoutEpilogue)) break;
       tc_fence_after();
       const int tile = unit / splits;
       const int split = unit % splits;
-      const int m0 = (tile % num_m) * kGemmBM;
-      const int n0 = (tile / num_m) * BN;
+      int mb, nb;
+      tile_coords(args, tile, mb, nb);
+      const int m0 = mb * kGemmBM;
+      const int n0 = nb * BN;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
       bool emit = true;
       if (splits > 1) {
@@ -584,6 +627,9 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.K = int(p.K);
   a.num_m_blk = int((p.M + kGemmBM - 1) / kGemmBM);
   const int num_n = int((p.N + bn - 1) / bn);
+  a.num_n_blk = num_n;
+  // Raster: keep the larger operand's tiles in L2 while the smaller one streams past them.
+  a.n_fastest = (p.M >= p.N) ? 1 : 0;
   const int64_t tiles = int64_t(a.num_m_blk) * num_n;
   if (tiles > INT32_MAX) return fail(kErrInvalid, "GEMM has too many tiles");
   a.num_tiles = int(tiles);
