@@ -58,23 +58,23 @@ struct AttnLayout {
   static constexpr int kKVAtom = BN * kAtomBytesPerRow;
   static constexpr int kQBytes = kNA * kQAtom;
   static constexpr int kKVBytes = kNA * kKVAtom;         // one K (or V) tile
-  static constexpr int kPAtoms = BN / 64;                // P: keys along K, 64 per atom
-  static constexpr int kPBytes = kPAtoms * kQAtom;
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQBytes;
   static constexpr int kVOff = kKOff + STAGES * kKVBytes;
-  static constexpr int kPOff = kVOff + STAGES * kKVBytes;
-  static constexpr int kBarOff = kPOff + 2 * kPBytes;
+  static constexpr int kBarOff = kVOff + STAGES * kKVBytes;
   // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_empty[2], p_full[2], pv_done[2], drain
   static constexpr int kNumBars = 1 + 3 * STAGES + 8 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + slack to align the base to 1 KB
   static constexpr int kSCol = 0;            // S[0] at column 0, S[1] at column BN
-  static constexpr int kOCol = 2 * BN;       // O accumulator
-  static constexpr int kTmemCols = (2 * BN + DP <= 256) ? 256 : 512;
+  static constexpr int kOCol = 2 * BN;       // O accumulator (DP columns)
+  // P[0], P[1]: bf16 pairs, BN/2 columns each (the A operand of P V), 32-column aligned.
+  static constexpr int kPCol = (2 * BN + DP + 31) / 32 * 32;
+  static constexpr int kTmemUsed = kPCol + BN;
+  static constexpr int kTmemCols = (kTmemUsed <= 128) ? 128 : (kTmemUsed <= 256) ? 256 : 512;
   static_assert(DP % 16 == 0 && DP >= 16 && DP <= 256, "padded head dim must be a multiple of 16 in [16, 256]");
-  static_assert(BN % 64 == 0 && BN <= 256, "key tile must be a multiple of 64 (one P atom)");
-  static_assert(2 * BN + DP <= 512, "S double buffer + O must fit in 512 TMEM columns");
+  static_assert(BN % 64 == 0 && BN <= 256, "key tile must be a multiple of 64");
+  static_assert(kTmemUsed <= 512, "S double buffer + O + P double buffer must fit in 512 TMEM columns");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -88,7 +88,8 @@ __device__ __forceinline__ void map_coords(const MapPos& p, int atom, int s, int
 }
 
 template <int DP, int BN, int STAGES>
-__global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSmemBytes <= 113 * 1024) ? 2 : 1)
+__global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSmemBytes <= 113 * 1024 &&
+                                                  AttnLayout<DP, BN, STAGES>::kTmemCols <= 256) ? 2 : 1)
     attention_fwd_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                                  const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
   using L = AttnLayout<DP, BN, STAGES>;
@@ -97,7 +98,6 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
   uint8_t* sQ = smem + L::kQOff;
   uint8_t* sK = smem + L::kKOff;
   uint8_t* sV = smem + L::kVOff;
-  uint8_t* sP = smem + L::kPOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
@@ -213,10 +213,11 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
       }
       if (ok && !mbar_wait_bounded(q_full, 0, abort_flag, args.ctl, kStatusTimeoutMma)) ok = false;
       tc_fence_after();
-      const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
-      const uint32_t k_addr = smem_u32(sK);
-      const uint32_t v_addr = smem_u32(sV);
+      // Descriptors are built once; every operand of every step is the base plus a byte offset (whose >> 4 lands in
+      // the descriptor's address field), so the issue loop is one 64-bit add per operand per MMA.
+      const uint64_t q_desc = smem_desc_kmajor_sw128(smem_u32(sQ));
+      const uint64_t k_desc = smem_desc_kmajor_sw128(smem_u32(sK));
+      const uint64_t v_desc = smem_desc_mnmajor_sw128(smem_u32(sV), L::kKVAtom);
       auto issue_pv = [&](int i) -> bool {
         const int st = i % STAGES;
         const uint32_t ph = uint32_t(i / STAGES) & 1u;
@@ -225,15 +226,14 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
         if (!mbar_wait_bounded(&p_full[buf], uint32_t(i >> 1) & 1u, abort_flag, args.ctl, kStatusTimeoutMma))
           return false;
         tc_fence_after();
-        const uint32_t pa = p_addr + buf * L::kPBytes;
-        const uint32_t va = v_addr + st * L::kKVBytes;
+        const uint32_t pa = tmem_base + uint32_t(L::kPCol + buf * (BN / 2));
+        const uint64_t va = v_desc + uint64_t((st * L::kKVBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          // P: K-major over keys, atoms of 64 keys, +32 B per 16 keys inside an atom.
-          const uint64_t a = smem_desc_kmajor_sw128(pa + (kk >> 2) * L::kQAtom + (kk & 3) * 32);
-          // V: MN-major (head dim contiguous), 16 keys = 16 rows of 128 B further per K step.
-          const uint64_t b = smem_desc_mnmajor_sw128(va + kk * 16 * kAtomBytesPerRow, L::kKVAtom);
-          umma_f16_ss(tmem_base + L::kOCol, a, b, kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
+          // P from TMEM: 16 keys = 8 columns per K step. V: MN-major (head dim contiguous), 16 keys = 16 rows of
+          // 128 B further per K step.
+          umma_f16_ts(tmem_base + L::kOCol, pa + uint32_t(kk * 8), va + uint64_t((kk * 16 * kAtomBytesPerRow) >> 4),
+                      kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&pv_done[buf]);
         umma_commit(&kv_empty[st]);
@@ -253,13 +253,12 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
           break;
         }
         tc_fence_after();
-        const uint32_t ka = k_addr + st * L::kKVBytes;
+        const uint64_t ka = k_desc + uint64_t((st * L::kKVBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < DP / 16; ++kk) {
           // Q and K: K-major over the head dim, atoms of 64 columns, +32 B per 16 columns inside an atom.
-          const uint64_t a = smem_desc_kmajor_sw128(q_addr + (kk >> 2) * L::kQAtom + (kk & 3) * 32);
-          const uint64_t b = smem_desc_kmajor_sw128(ka + (kk >> 2) * L::kKVAtom + (kk & 3) * 32);
-          umma_f16_ss(tmem_base + L::kSCol + buf * BN, a, b, kIdescS, kk > 0 ? 1u : 0u);
+          umma_f16_ss(tmem_base + L::kSCol + buf * BN, q_desc + uint64_t(((kk >> 2) * L::kQAtom + (kk & 3) * 32) >> 4),
+                      ka + uint64_t(((kk >> 2) * L::kKVAtom + (kk & 3) * 32) >> 4), kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[buf]);
         if (j >= 1 && !issue_pv(j - 1)) {
@@ -333,22 +332,20 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
         ok = false;
         break;
       }
-      // P row: 16-byte chunks of 8 keys, chunk q of an atom stored at (q ^ row % 8) (the 128-byte swizzle).
-      uint8_t* prow = sP + buf * L::kPBytes + row * kAtomBytesPerRow;
+      // P row into TMEM (this thread's lane): bf16 pairs, 32 keys = 16 columns per store.
+      const uint32_t p_cols = lane_base + uint32_t(L::kPCol + buf * (BN / 2));
 #pragma unroll
-      for (int ch = 0; ch < BN / 8; ++ch) {
-        float p[8];
+      for (int c32 = 0; c32 < BN / 32; ++c32) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          p[e] = fast_exp2(fmaf(s[ch * 8 + e], c, neg_m));
-          rs8[e] += p[e];
+        for (int e2 = 0; e2 < 16; ++e2) {
+          const float p0 = fast_exp2(fmaf(s[c32 * 32 + 2 * e2], c, neg_m));
+          const float p1 = fast_exp2(fmaf(s[c32 * 32 + 2 * e2 + 1], c, neg_m));
+          rs8[(2 * e2) & 7] += p0;
+          rs8[(2 * e2 + 1) & 7] += p1;
+          pk[e2] = pack_bf16x2(p0, p1);
         }
-        uint4 v;
-        v.x = pack_bf16x2(p[0], p[1]);
-        v.y = pack_bf16x2(p[2], p[3]);
-        v.z = pack_bf16x2(p[4], p[5]);
-        v.w = pack_bf16x2(p[6], p[7]);
-        *reinterpret_cast<uint4*>(prow + (ch >> 3) * L::kQAtom + (((ch & 7) ^ (row & 7)) << 4)) = v;
+        tmem_st16(p_cols + uint32_t(c32 * 16), pk);
       }
 #pragma unroll
       for (int w = 4; w >= 1; w >>= 1)
@@ -376,7 +373,7 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
         }
         tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[buf]);
