@@ -10,7 +10,7 @@ The nodes are registered under the reference's class names too, so saved workflo
 
 What changes: the model runs on the GPU, so calls route by device `cuda` (the reference routes CPU tensors to the
 NPU, node :150, :174). The attention gate no longer chooses between the accelerator and the CPU: it chooses
-between kernel variants of the fused attention (key tile 128 or 64) by timing each once per shape, and still
+between kernel variants of the fused attention (query tiles per CTA x key tile) by timing each once per shape, and still
 checks the first result of every shape against the model's own attention (max relative error <= 0.1, else
 RuntimeError, node :225-232). Shapes with a mask or GQA (which the fused kernel does not implement) and
 attention mode "off" (the reference's "cpu") run the model's own attention function, logged once per shape.
@@ -27,7 +27,15 @@ import torch
 _RUNTIME = None
 _RUNTIME_LOCK = threading.RLock()
 ATTENTION_MODES = ["auto", "gpu", "off", "npu", "cpu"]   # "npu" / "cpu": the reference's names for gpu / off
-ATTN_VARIANTS = (128, 64)
+
+
+def attn_variants(head_dim: int) -> tuple[int, ...]:
+    """Fused-attention variants the gate times for a head dim: 0 (the kernel's own measured choice) first, then
+    every distinct (query tiles per CTA, key tile) pair the head dim allows, encoded as 1000 * tiles + keys."""
+    dp = (head_dim + 15) // 16 * 16
+    keys = (64, 96, 128) if dp <= 64 else ((64, 128) if dp <= 128 else (64,))
+    qts = (1, 2) if dp <= 192 else (1,)
+    return (0,) + tuple(1000 * qt + bn for qt in qts for bn in keys)
 
 
 def _log(msg: str) -> None:
@@ -82,7 +90,7 @@ class AttentionGate:
         rows = []
         for key in sorted(set(self.ms) | set(self.reason)):
             d = self.decision.get(key, self.reason.get(key, "pending"))
-            row = f"{key}: " + ", ".join(f"tile{v} {t:.3f} ms" for v, t in sorted(self.ms.get(key, {}).items()))
+            row = f"{key}: " + ", ".join(f"variant {v} {t:.3f} ms" for v, t in sorted(self.ms.get(key, {}).items()))
             if key in self.ref_ms:
                 row += f", model {self.ref_ms[key]:.3f} ms"
             if key in self.max_err:
@@ -205,7 +213,7 @@ def _gpu_attention_override(func, q, k, v, heads, mask=None, attn_precision=None
     decision = gate.decision.get(key)
     if decision is None:
         # First call of this shape: time the variants, check against the model's own attention once.
-        variants = ATTN_VARIANTS if gate.mode == "auto" else ATTN_VARIANTS[:1]
+        variants = attn_variants(d) if gate.mode == "auto" else (0,)
         y = None
         for var in variants:
             fused(var)  # warm-up
@@ -222,8 +230,8 @@ def _gpu_attention_override(func, q, k, v, heads, mask=None, attn_precision=None
                                f"(max rel err {err:.3g})")
         decision = min(gate.ms[key], key=gate.ms[key].get)
         gate.decision[key] = decision
-        _log(f"attention gate {key}: " + ", ".join(f"tile{v} {t:.3f} ms" for v, t in sorted(gate.ms[key].items()))
-             + f" (model's own {ref_ms:.3f} ms), max rel err {err:.1e} -> tile{decision}")
+        _log(f"attention gate {key}: " + ", ".join(f"variant {v} {t:.3f} ms" for v, t in sorted(gate.ms[key].items()))
+             + f" (model's own {ref_ms:.3f} ms), max rel err {err:.1e} -> variant {decision}")
     t0 = time.perf_counter()
     y = fused(decision)
     gate.gpu_seconds += time.perf_counter() - t0

@@ -10,18 +10,29 @@
 // (K/V interleaving, Q slabs, parts), its tiling limits (tq % 4bq, tk % bk, bh % 4; xdna1_program.py:422-426) and
 // the per-head fallback: any Sq/Skv works here, the key tail (e.g. Skv = 77) is masked in the kernel.
 //
-// One CTA per (128-query tile, (b, h) pair); 192 threads:
-//   warps 0-3   softmax: thread t owns query row t of the tile = TMEM lane t. Reads its S row from TMEM,
-//               masks the key tail, keeps the running max m and sum l in registers, writes P (bf16) to shared
-//               memory, rescales its O row in TMEM when m moves, and normalises + stores O at the end.
-//   warp 4      TMA producer: Q once, then K and V tiles into a STAGES-deep ring.
-//   warp 5      TMEM owner + MMA issuer: S[j%2] = Q K_j^T (tcgen05, M=128, N=BN), then O += P_{j-1} V_{j-1}, so the
-//               tensor core computes the next scores while the softmax works on the current ones.
+// Two kernels share one structure (softmax warps, a TMA producer warp, an MMA warp) and differ in how many
+// 128-row query tiles a CTA owns:
+//   attention_fwd_qt2_tcgen05_kernel  two Q tiles (256 query rows) per CTA, one CTA per SM, 320 threads. Both tiles
+//       share every K/V tile, and one MMA thread per SM feeds the tensor core, so MMA issue never contends with
+//       another CTA's. Per key tile j the MMA order is P_0(j-1) V, S_0(j), P_1(j-1) V, S_1(j): while softmax
+//       warpgroup 0 works on S_0(j), the tensor core finishes tile 1's work and the other way round.
+//   attention_fwd_tcgen05_kernel      one Q tile per CTA with S double-buffered (S_j, S_{j+1}), 192 threads, up to
+//       two CTAs per SM: for grids too small to fill the GPU with 256-row CTAs, and head dims above 192.
+// Roles:
+//   softmax warps  thread t of a warpgroup owns query row t of its Q tile = TMEM lane t. Reads its S row from TMEM,
+//                  masks the key tail, keeps the running max m and sum l in registers, writes P (bf16 pairs) back
+//                  into the TMEM columns its S tile came from (the A operand of P V), rescales its O row in TMEM
+//                  when m moves, and normalises + stores O at the end.
+//   producer warp  TMA: Q once, then K and V tiles into STAGES-deep rings, K one tile ahead of V. A K slot is
+//                  released as soon as its S MMAs complete, a V slot when its P V MMAs complete.
+//   MMA warp       TMEM owner + tcgen05 issuer: S = Q K_j^T (M=128, N=BN, both K-major in shared memory) and
+//                  O += P V_j (P from TMEM, V MN-major in shared memory). tcgen05.mma ops of one thread execute in
+//                  issue order, so S_{j+1} (or S_{j+2}) may overwrite the columns holding P_j once P_j V_j has been
+//                  issued, and a tcgen05.commit covers every MMA issued before it.
 // Data layout: every operand lives in shared memory as 128-byte-swizzled atoms of 64 head-dim (or key) columns,
 // loaded by TMA with 128-byte rows from a 4-D (dim, head, seq, batch) tensor map over the caller's strided
 // tensor. The map's innermost extent is the true head dim, so the columns past it (40 -> 64, 80 -> 128,
-// 160 -> 192) come in as TMA's out-of-bounds zeros: no host padding, no copies of the model's tensors, and the
-// tensor core reads K-major Q/K/P and MN-major V straight from those atoms.
+// 160 -> 192) come in as TMA's out-of-bounds zeros: no host padding, no copies of the model's tensors.
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -30,10 +41,16 @@
 
 namespace npub200 {
 
-constexpr int kAttnBM = 128;
-constexpr int kAttnThreads = 192;
-constexpr int kSoftmaxWarps = 4;
+constexpr int kAttnBM = 128;           // query rows per Q tile (one softmax warpgroup, one TMEM lane per row)
+constexpr int kSoftmaxWarps = 4;       // per Q tile
 constexpr int kAtomBytesPerRow = 128;  // one 128-byte swizzle atom row: 64 bf16
+// Of every 8 (key, key+1) pairs of a softmax row, this many take their exponentials from the FMA-pipe polynomial
+// (exp2_poly3) instead of the MUFU. Head dims up to 64 (the least MMA work per exponential) gain from moving 2 of 8
+// to the FP32 pipe; larger head dims measured best with none.
+template <int DP>
+constexpr int exp_poly_pairs_per8() {
+  return DP <= 64 ? 2 : 0;
+}
 
 struct MapPos {
   int s, h, b;  // position (1..3) of the seq / head / batch dimension in the tensor map
@@ -51,33 +68,6 @@ struct AttnArgs {
   KernelCtl ctl;
 };
 
-template <int DP, int BN, int STAGES>
-struct AttnLayout {
-  static constexpr int kNA = (DP + 63) / 64;             // 64-column atoms along the head dim
-  static constexpr int kQAtom = kAttnBM * kAtomBytesPerRow;  // 16 KB
-  static constexpr int kKVAtom = BN * kAtomBytesPerRow;
-  static constexpr int kQBytes = kNA * kQAtom;
-  static constexpr int kKVBytes = kNA * kKVAtom;         // one K (or V) tile
-  static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kQBytes;
-  static constexpr int kVOff = kKOff + STAGES * kKVBytes;
-  static constexpr int kBarOff = kVOff + STAGES * kKVBytes;
-  // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_empty[2], p_full[2], pv_done[2], drain
-  static constexpr int kNumBars = 1 + 3 * STAGES + 8 + 1;
-  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + slack to align the base to 1 KB
-  static constexpr int kSCol = 0;            // S[0] at column 0, S[1] at column BN
-  static constexpr int kOCol = 2 * BN;       // O accumulator (DP columns)
-  // P[0], P[1]: bf16 pairs, BN/2 columns each (the A operand of P V), 32-column aligned.
-  static constexpr int kPCol = (2 * BN + DP + 31) / 32 * 32;
-  static constexpr int kTmemUsed = kPCol + BN;
-  static constexpr int kTmemCols = (kTmemUsed <= 128) ? 128 : (kTmemUsed <= 256) ? 256 : 512;
-  static_assert(DP % 16 == 0 && DP >= 16 && DP <= 256, "padded head dim must be a multiple of 16 in [16, 256]");
-  static_assert(BN % 64 == 0 && BN <= 256, "key tile must be a multiple of 64");
-  static_assert(kTmemUsed <= 512, "S double buffer + O + P double buffer must fit in 512 TMEM columns");
-  static_assert(kSmemBytes <= 232448, "shared memory budget");
-};
-
 // Coordinates (dim, then the three outer dims in the map's order) of 64-column atom `atom` of row s of (b, h).
 __device__ __forceinline__ void map_coords(const MapPos& p, int atom, int s, int h, int b, int& c0, int& c1, int& c2,
                                            int& c3) {
@@ -87,12 +77,265 @@ __device__ __forceinline__ void map_coords(const MapPos& p, int atom, int s, int
   c3 = p.s == 3 ? s : (p.h == 3 ? h : b);
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Producer: K and V tiles of one (b, h) pair into STAGES-deep rings, K one tile ahead of V (K_j is needed a whole
+// softmax step before V_j). On an abort it waits for the loads it issued before returning, so shared memory is
+// not released under an in-flight copy.
+// ---------------------------------------------------------------------------------------------------------------
+template <int NA, int BN, int STAGES>
+__device__ __forceinline__ void kv_producer(const CUtensorMap* tm_k, const CUtensorMap* tm_v, const AttnArgs& args,
+                                            uint8_t* sK, uint8_t* sV, uint64_t* k_full, uint64_t* v_full,
+                                            uint64_t* k_empty, uint64_t* v_empty, volatile int* abort_flag, int hh,
+                                            int bb) {
+  constexpr int kAtom = BN * kAtomBytesPerRow;
+  constexpr int kTile = NA * kAtom;
+  const int nkv = args.nkv;
+  int issued_k = 0, issued_v = 0;
+  bool ok = true;
+  int c0, c1, c2, c3;
+  for (int j = 0; j <= nkv; ++j) {
+    if (j < nkv) {
+      const int st = j % STAGES;
+      if (!mbar_wait_bounded(&k_empty[st], (uint32_t(j / STAGES) & 1u) ^ 1u, abort_flag, args.ctl,
+                             kStatusTimeoutProducer)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive_expect_tx(&k_full[st], kTile);
+      for (int a = 0; a < NA; ++a) {
+        map_coords(args.pk, a, j * BN, hh, bb, c0, c1, c2, c3);
+        tma_load_4d(tm_k, &k_full[st], sK + st * kTile + a * kAtom, c0, c1, c2, c3);
+      }
+      ++issued_k;
+    }
+    if (j >= 1) {
+      const int i = j - 1;
+      const int st = i % STAGES;
+      if (!mbar_wait_bounded(&v_empty[st], (uint32_t(i / STAGES) & 1u) ^ 1u, abort_flag, args.ctl,
+                             kStatusTimeoutProducer)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive_expect_tx(&v_full[st], kTile);
+      for (int a = 0; a < NA; ++a) {
+        map_coords(args.pv, a, i * BN, hh, bb, c0, c1, c2, c3);
+        tma_load_4d(tm_v, &v_full[st], sV + st * kTile + a * kAtom, c0, c1, c2, c3);
+      }
+      ++issued_v;
+    }
+  }
+  if (!ok) {
+    for (int i = max(0, issued_k - STAGES); i < issued_k; ++i)
+      mbar_wait_drain(&k_full[i % STAGES], uint32_t(i / STAGES) & 1u, args.ctl);
+    for (int i = max(0, issued_v - STAGES); i < issued_v; ++i)
+      mbar_wait_drain(&v_full[i % STAGES], uint32_t(i / STAGES) & 1u, args.ctl);
+  }
+}
+
+// S = Q K_j^T for one Q tile: K-major over the head dim, atoms of 64 columns, +32 B per 16 columns in an atom.
+template <int DP, int BN>
+__device__ __forceinline__ void issue_s(uint32_t d_tmem, uint64_t q_desc, uint64_t k_desc, int q_atom_bytes,
+                                        int kv_atom_bytes) {
+  constexpr uint32_t kIdescS = idesc_bf16_f32(kAttnBM, BN, false);
+#pragma unroll
+  for (int kk = 0; kk < DP / 16; ++kk)
+    umma_f16_ss(d_tmem, q_desc + uint64_t(((kk >> 2) * q_atom_bytes + (kk & 3) * 32) >> 4),
+                k_desc + uint64_t(((kk >> 2) * kv_atom_bytes + (kk & 3) * 32) >> 4), kIdescS, kk > 0 ? 1u : 0u);
+}
+
+// O += P V_j: P from TMEM (16 keys = 8 columns of bf16 pairs per K step), V MN-major (head dim contiguous), 16 keys
+// = 16 rows of 128 B further per K step.
+template <int DP, int BN>
+__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint64_t v_desc, bool accumulate) {
+  constexpr uint32_t kIdescO = idesc_bf16_f32(kAttnBM, DP, true);
+#pragma unroll
+  for (int kk = 0; kk < BN / 16; ++kk)
+    umma_f16_ts(o_tmem, p_tmem + uint32_t(kk * 8), v_desc + uint64_t((kk * 16 * kAtomBytesPerRow) >> 4), kIdescO,
+                (accumulate || kk > 0) ? 1u : 0u);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Softmax-warp pieces shared by both kernels. A softmax thread owns one query row = one TMEM lane.
+// ---------------------------------------------------------------------------------------------------------------
+
+// One online-softmax step over a key tile for this thread's row: reads the BN scores (TMEM columns from s_addr),
+// masks keys >= Skv, moves the running max m lazily (only when the tile's max beats it by more than thr, log2
+// units), writes P = exp2(s*c - m) as bf16 pairs over the first BN/2 of those columns and updates the running
+// sum l. Returns the factor O must be scaled by (1 when m did not move); `move` tells whether it moved. The caller
+// signals P once its stores are complete (tmem_wait_st).
+template <int BN, int POLY>
+__device__ __forceinline__ float softmax_step(uint32_t s_addr, int kv0, int Skv, float c, float thr, float& m,
+                                              float& l, bool& move) {
+  float s[BN];  // raw scores of this row (the scale is folded into the exponent below)
+#pragma unroll
+  for (int cc = 0; cc < BN; cc += 32) {
+    uint32_t r[32];
+    tmem_ld32(s_addr + uint32_t(cc), r);
+#pragma unroll
+    for (int t = 0; t < 32; ++t) s[cc + t] = __uint_as_float(r[t]);
+  }
+  tmem_wait_ld();
+  if (kv0 + BN > Skv) {
+#pragma unroll
+    for (int t = 0; t < BN; ++t)
+      if (kv0 + t >= Skv) s[t] = -INFINITY;
+  }
+  // Row max as 8 independent chains of three-input maxima, then a two-level tree.
+  float mx8[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) mx8[e] = s[e];
+#pragma unroll
+  for (int t = 8; t + 16 <= BN; t += 16)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mx8[e] = fmax3(mx8[e], s[t + e], s[t + 8 + e]);
+  if constexpr ((BN - 8) % 16 != 0) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mx8[e] = fmaxf(mx8[e], s[BN - 8 + e]);
+  }
+  const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])) *
+                   c;  // log2 units (c = scale * log2 e > 0)
+  move = mx > m + thr;
+  const float m_new = move ? mx : m;
+  const float alpha = fast_exp2(m - m_new);  // 1 when unchanged, 0 on the first tile
+  const float neg_m = -m_new;
+  float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  // P row into TMEM over this lane's S (already in registers): bf16 pairs, 32 keys = 16 columns per store.
+#pragma unroll
+  for (int c32 = 0; c32 < BN / 32; ++c32) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int e2 = 0; e2 < 16; ++e2) {
+      const float x0 = fmaf(s[c32 * 32 + 2 * e2], c, neg_m);
+      const float x1 = fmaf(s[c32 * 32 + 2 * e2 + 1], c, neg_m);
+      const bool poly = (e2 & 7) >= 8 - POLY;
+      const float p0 = poly ? exp2_poly3(x0) : fast_exp2(x0);
+      const float p1 = poly ? exp2_poly3(x1) : fast_exp2(x1);
+      rs8[(2 * e2) & 7] += p0;
+      rs8[(2 * e2 + 1) & 7] += p1;
+      pk[e2] = pack_bf16x2(p0, p1);
+    }
+    tmem_st16(s_addr + uint32_t(c32 * 16), pk);
+  }
+#pragma unroll
+  for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+    for (int e = 0; e < w; ++e) rs8[e] += rs8[e + w];
+  l = l * alpha + rs8[0];
+  m = m_new;
+  return alpha;
+}
+
+// O row *= alpha (TMEM columns from o_addr). Warp-wide: lanes whose max did not move pass alpha = 1.
+template <int DP>
+__device__ __forceinline__ void rescale_o_row(uint32_t o_addr, float alpha) {
+#pragma unroll
+  for (int cc = 0; cc < DP; cc += 16) {
+    uint32_t r[16];
+    tmem_ld16(o_addr + uint32_t(cc), r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int t = 0; t < 16; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
+    tmem_st16(o_addr + uint32_t(cc), r);
+  }
+  tmem_wait_st();
+}
+
+// Normalised O row (TMEM columns from o_addr) to the output: the first D columns of row `grow` of pair (bb, hh),
+// bf16 or f32, 16-byte vector stores where aligned. Rows past Sq only drain TMEM (tcgen05.ld is warp-wide).
+template <int DP>
+__device__ __forceinline__ void store_o_row(uint32_t o_addr, const AttnArgs& args, int grow, int bb, int hh,
+                                            float inv_l) {
+  const bool store = grow < args.Sq;
+  const long long obase = (long long)bb * args.o_sb + (long long)grow * args.o_ss + (long long)hh * args.o_sh;
+#pragma unroll
+  for (int cc = 0; cc < DP; cc += 16) {
+    uint32_t r[16];
+    tmem_ld16(o_addr + uint32_t(cc), r);
+    tmem_wait_ld();
+    if (store) {
+      float o[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t) o[t] = __uint_as_float(r[t]) * inv_l;
+      const int ncols = min(16, args.D - cc);
+      if (args.out_f32) {
+        float* dst = static_cast<float*>(args.out) + obase + cc;
+        if (ncols == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            reinterpret_cast<float4*>(dst)[t] = make_float4(o[4 * t], o[4 * t + 1], o[4 * t + 2], o[4 * t + 3]);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 16; ++t)
+            if (t < ncols) dst[t] = o[t];
+        }
+      } else {
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(args.out) + obase + cc;
+        if (ncols >= 8 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+          uint4 v0;
+          v0.x = pack_bf16x2(o[0], o[1]);
+          v0.y = pack_bf16x2(o[2], o[3]);
+          v0.z = pack_bf16x2(o[4], o[5]);
+          v0.w = pack_bf16x2(o[6], o[7]);
+          reinterpret_cast<uint4*>(dst)[0] = v0;
+          if (ncols == 16) {
+            uint4 v1;
+            v1.x = pack_bf16x2(o[8], o[9]);
+            v1.y = pack_bf16x2(o[10], o[11]);
+            v1.z = pack_bf16x2(o[12], o[13]);
+            v1.w = pack_bf16x2(o[14], o[15]);
+            reinterpret_cast<uint4*>(dst)[1] = v1;
+          } else {
+#pragma unroll
+            for (int t = 8; t < 16; ++t)
+              if (t < ncols) dst[t] = __float2bfloat16_rn(o[t]);
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 16; ++t)
+            if (t < ncols) dst[t] = __float2bfloat16_rn(o[t]);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Kernel 1: one Q tile per CTA, S double-buffered. Warps 0-3 softmax, warp 4 producer, warp 5 MMA.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kAttn1Threads = 192;
+
 template <int DP, int BN, int STAGES>
-__global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSmemBytes <= 113 * 1024 &&
-                                                  AttnLayout<DP, BN, STAGES>::kTmemCols <= 256) ? 2 : 1)
+struct Attn1Layout {
+  static constexpr int kNA = (DP + 63) / 64;                 // 64-column atoms along the head dim
+  static constexpr int kQAtom = kAttnBM * kAtomBytesPerRow;  // 16 KB
+  static constexpr int kKVAtom = BN * kAtomBytesPerRow;
+  static constexpr int kQBytes = kNA * kQAtom;
+  static constexpr int kKVBytes = kNA * kKVAtom;  // one K (or V) tile
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = kQOff + kQBytes;
+  static constexpr int kVOff = kKOff + STAGES * kKVBytes;
+  static constexpr int kBarOff = kVOff + STAGES * kKVBytes;
+  // q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], p_full[2], pv_done[2], drain
+  static constexpr int kNumBars = 1 + 4 * STAGES + 6 + 1;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + slack to align the base to 1 KB
+  // S[0] at column 0, S[1] at column BN; P_j overwrites the first half of its own S buffer; O after them.
+  static constexpr int kSCol = 0;
+  static constexpr int kOCol = 2 * BN;
+  static constexpr int kTmemUsed = kOCol + DP;
+  static constexpr int kTmemCols = (kTmemUsed <= 128) ? 128 : (kTmemUsed <= 256) ? 256 : 512;
+  static constexpr bool kTwoPerSm = kSmemBytes <= 113 * 1024 && kTmemCols <= 256;
+  static_assert(DP % 16 == 0 && DP >= 16 && DP <= 256, "padded head dim must be a multiple of 16 in [16, 256]");
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "key tile must be a multiple of 32 in [64, 256]");
+  static_assert(kTmemUsed <= 512, "S double buffer + O must fit in 512 TMEM columns");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+template <int DP, int BN, int STAGES>
+__global__ void __launch_bounds__(kAttn1Threads, Attn1Layout<DP, BN, STAGES>::kTwoPerSm ? 2 : 1)
     attention_fwd_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                                  const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
-  using L = AttnLayout<DP, BN, STAGES>;
+  using L = Attn1Layout<DP, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::kQOff;
@@ -102,10 +345,10 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + STAGES;
-  uint64_t* kv_empty = v_full + STAGES;
-  uint64_t* s_full = kv_empty + STAGES;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
+  uint64_t* k_empty = v_full + STAGES;
+  uint64_t* v_empty = k_empty + STAGES;
+  uint64_t* s_full = v_empty + STAGES;
+  uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = p_full + 2;
   uint64_t* drain = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
@@ -124,11 +367,11 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kSoftmaxWarps);
       mbar_init(&p_full[i], kSoftmaxWarps);
       mbar_init(&pv_done[i], 1);
     }
@@ -159,122 +402,71 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
         map_coords(args.pq, a, q0, hh, bb, c0, c1, c2, c3);
         tma_load_4d(&tm_q, q_full, sQ + a * L::kQAtom, c0, c1, c2, c3);
       }
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued = 0;
-      bool ok = true;
-      for (int j = 0; j < nkv; ++j) {
-        if (!mbar_wait_bounded(&kv_empty[stage], phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutProducer)) {
-          ok = false;
-          break;
-        }
-        const int kv0 = j * BN;
-        mbar_arrive_expect_tx(&k_full[stage], L::kKVBytes);
-        for (int a = 0; a < L::kNA; ++a) {
-          map_coords(args.pk, a, kv0, hh, bb, c0, c1, c2, c3);
-          tma_load_4d(&tm_k, &k_full[stage], sK + stage * L::kKVBytes + a * L::kKVAtom, c0, c1, c2, c3);
-        }
-        mbar_arrive_expect_tx(&v_full[stage], L::kKVBytes);
-        for (int a = 0; a < L::kNA; ++a) {
-          map_coords(args.pv, a, kv0, hh, bb, c0, c1, c2, c3);
-          tma_load_4d(&tm_v, &v_full[stage], sV + stage * L::kKVBytes + a * L::kKVAtom, c0, c1, c2, c3);
-        }
-        ++issued;
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-      // Drain: Q and the loads of the last min(issued, STAGES) tiles must land before shared memory is released.
+      kv_producer<L::kNA, BN, STAGES>(&tm_k, &tm_v, args, sK, sV, k_full, v_full, k_empty, v_empty, abort_flag, hh,
+                                      bb);
       mbar_wait_drain(q_full, 0, args.ctl);
-      if (!ok) {
-        int s = stage;
-        uint32_t ph = phase;
-        for (int i = 0; i < min(issued, STAGES); ++i) {
-          if (s == 0) {
-            s = STAGES - 1;
-            ph ^= 1u;
-          } else {
-            --s;
-          }
-          mbar_wait_drain(&k_full[s], ph, args.ctl);
-          mbar_wait_drain(&v_full[s], ph, args.ctl);
-        }
-      }
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kIdescS = idesc_bf16_f32(kAttnBM, BN, false);  // S = Q K^T: both K-major
-      constexpr uint32_t kIdescO = idesc_bf16_f32(kAttnBM, DP, true);   // O += P V: V is MN-major
-      bool ok = true;
-      if (args.ctl.debug & 1u) {
-        if (!mbar_wait_bounded(drain, 0, abort_flag, args.ctl, kStatusForced)) ok = false;
-      }
-      if (ok && !mbar_wait_bounded(q_full, 0, abort_flag, args.ctl, kStatusTimeoutMma)) ok = false;
+    // The whole warp runs the loop (operands stay warp-uniform); one elected lane issues the MMAs and their commits.
+    bool ok = true;
+    if (args.ctl.debug & 1u) {
+      if (!mbar_wait_bounded_warp(drain, 0, abort_flag, args.ctl, kStatusForced)) ok = false;
+    }
+    if (ok && !mbar_wait_bounded_warp(q_full, 0, abort_flag, args.ctl, kStatusTimeoutMma)) ok = false;
+    tc_fence_after();
+    // Descriptors are built once; every operand of every step is the base plus a byte offset (whose >> 4 lands in
+    // the descriptor's address field).
+    const uint64_t q_desc = smem_desc_kmajor_sw128(smem_u32(sQ));
+    const uint64_t k_desc = smem_desc_kmajor_sw128(smem_u32(sK));
+    const uint64_t v_desc = smem_desc_mnmajor_sw128(smem_u32(sV), L::kKVAtom);
+    auto pv_step = [&](int i) -> bool {
+      const int st = i % STAGES;
+      const int buf = i & 1;
+      if (!mbar_wait_bounded_warp(&v_full[st], uint32_t(i / STAGES) & 1u, abort_flag, args.ctl, kStatusTimeoutMma))
+        return false;
+      if (!mbar_wait_bounded_warp(&p_full[buf], uint32_t(i >> 1) & 1u, abort_flag, args.ctl, kStatusTimeoutMma))
+        return false;
       tc_fence_after();
-      // Descriptors are built once; every operand of every step is the base plus a byte offset (whose >> 4 lands in
-      // the descriptor's address field), so the issue loop is one 64-bit add per operand per MMA.
-      const uint64_t q_desc = smem_desc_kmajor_sw128(smem_u32(sQ));
-      const uint64_t k_desc = smem_desc_kmajor_sw128(smem_u32(sK));
-      const uint64_t v_desc = smem_desc_mnmajor_sw128(smem_u32(sV), L::kKVAtom);
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % STAGES;
-        const uint32_t ph = uint32_t(i / STAGES) & 1u;
-        const int buf = i & 1;
-        if (!mbar_wait_bounded(&v_full[st], ph, abort_flag, args.ctl, kStatusTimeoutMma)) return false;
-        if (!mbar_wait_bounded(&p_full[buf], uint32_t(i >> 1) & 1u, abort_flag, args.ctl, kStatusTimeoutMma))
-          return false;
-        tc_fence_after();
-        const uint32_t pa = tmem_base + uint32_t(L::kPCol + buf * (BN / 2));
-        const uint64_t va = v_desc + uint64_t((st * L::kKVBytes) >> 4);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          // P from TMEM: 16 keys = 8 columns per K step. V: MN-major (head dim contiguous), 16 keys = 16 rows of
-          // 128 B further per K step.
-          umma_f16_ts(tmem_base + L::kOCol, pa + uint32_t(kk * 8), va + uint64_t((kk * 16 * kAtomBytesPerRow) >> 4),
-                      kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
-        }
+      if (elect_one()) {
+        issue_pv<DP, BN>(tmem_base + L::kOCol, tmem_base + uint32_t(L::kSCol + buf * BN),
+                         v_desc + uint64_t((st * L::kKVBytes) >> 4), i > 0);
         umma_commit(&pv_done[buf]);
-        umma_commit(&kv_empty[st]);
-        return true;
-      };
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j % STAGES;
-        const uint32_t ph = uint32_t(j / STAGES) & 1u;
-        const int buf = j & 1;
-        if (!mbar_wait_bounded(&k_full[st], ph, abort_flag, args.ctl, kStatusTimeoutMma)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait_bounded(&s_empty[buf], (uint32_t(j >> 1) & 1u) ^ 1u, abort_flag, args.ctl,
-                               kStatusTimeoutMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint64_t ka = k_desc + uint64_t((st * L::kKVBytes) >> 4);
-#pragma unroll
-        for (int kk = 0; kk < DP / 16; ++kk) {
-          // Q and K: K-major over the head dim, atoms of 64 columns, +32 B per 16 columns inside an atom.
-          umma_f16_ss(tmem_base + L::kSCol + buf * BN, q_desc + uint64_t(((kk >> 2) * L::kQAtom + (kk & 3) * 32) >> 4),
-                      ka + uint64_t(((kk >> 2) * L::kKVAtom + (kk & 3) * 32) >> 4), kIdescS, kk > 0 ? 1u : 0u);
-        }
+        umma_commit(&v_empty[st]);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int j = 0; ok && j < nkv; ++j) {
+      const int st = j % STAGES;
+      const int buf = j & 1;
+      if (!mbar_wait_bounded_warp(&k_full[st], uint32_t(j / STAGES) & 1u, abort_flag, args.ctl, kStatusTimeoutMma)) {
+        ok = false;
+        break;
+      }
+      // S[buf] is free: the softmax read S_{j-2} before it wrote P_{j-2} there (p_full), and P_{j-2} V_{j-2} was
+      // issued before this MMA.
+      tc_fence_after();
+      if (elect_one()) {
+        issue_s<DP, BN>(tmem_base + uint32_t(L::kSCol + buf * BN), q_desc, k_desc + uint64_t((st * L::kKVBytes) >> 4),
+                        L::kQAtom, L::kKVAtom);
         umma_commit(&s_full[buf]);
-        if (j >= 1 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
-        }
+        umma_commit(&k_empty[st]);
       }
-      if (ok && nkv >= 1 && !issue_pv(nkv - 1)) ok = false;
-      if (!ok) {
-        umma_commit(drain);
-        mbar_wait_drain(drain, 0u, args.ctl);
+      __syncwarp();
+      if (j >= 1 && !pv_step(j - 1)) {
+        ok = false;
+        break;
       }
+    }
+    if (ok && nkv >= 1 && !pv_step(nkv - 1)) ok = false;
+    if (!ok) {
+      if (elect_one()) umma_commit(drain);
+      __syncwarp();
+      mbar_wait_drain(drain, 0u, args.ctl);
     }
   } else {
     // ------------------------------------------------------------------ softmax / correction / epilogue (warps 0-3)
-    const int row = warp * 32 + lane;  // query row in the tile == TMEM lane
     const uint32_t lane_base = tmem_base + (uint32_t(warp * 32) << 16);
     const float c = args.scale_log2;
     float m = -INFINITY;  // running max in log2 units (scores * scale * log2 e)
@@ -287,74 +479,11 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
         break;
       }
       tc_fence_after();
-      float s[BN];  // raw scores of this row (the scale is folded into the exponent below)
-#pragma unroll
-      for (int cc = 0; cc < BN; cc += 32) {
-        uint32_t r[32];
-        tmem_ld32(lane_base + uint32_t(L::kSCol + buf * BN + cc), r);
-#pragma unroll
-        for (int t = 0; t < 32; ++t) s[cc + t] = __uint_as_float(r[t]);
-      }
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[buf]);
-
-      const int kv0 = j * BN;
-      if (kv0 + BN > args.Skv) {
-#pragma unroll
-        for (int t = 0; t < BN; ++t)
-          if (kv0 + t >= args.Skv) s[t] = -INFINITY;
-      }
-      // Row max as 8 independent chains, then a 3-level tree (short dependency chains keep the pipes busy).
-      float mx8[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) mx8[e] = s[e];
-#pragma unroll
-      for (int t = 8; t < BN; t += 8)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) mx8[e] = fmaxf(mx8[e], s[t + e]);
-#pragma unroll
-      for (int w = 4; w >= 1; w >>= 1)
-#pragma unroll
-        for (int e = 0; e < w; ++e) mx8[e] = fmaxf(mx8[e], mx8[e + w]);
-      const float mx = mx8[0] * c;  // log2 units (c = scale * log2 e > 0)
-      // Lazy running max: move only when this tile's max beats it by more than the threshold.
-      const bool move = mx > m + args.rescale_thr;
-      const float m_new = move ? mx : m;
-      const float alpha = fast_exp2(m - m_new);  // 1 when unchanged, 0 on the first tile
-      const float neg_m = -m_new;
-      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      // P buffer `buf` is free once PV of tile j-2 has completed.
-      if (j >= 2 &&
-          !mbar_wait_bounded(&pv_done[buf], (uint32_t((j - 2) >> 1) & 1u), abort_flag, args.ctl,
-                             kStatusTimeoutEpilogue)) {
-        ok = false;
-        break;
-      }
-      // P row into TMEM (this thread's lane): bf16 pairs, 32 keys = 16 columns per store.
-      const uint32_t p_cols = lane_base + uint32_t(L::kPCol + buf * (BN / 2));
-#pragma unroll
-      for (int c32 = 0; c32 < BN / 32; ++c32) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int e2 = 0; e2 < 16; ++e2) {
-          const float p0 = fast_exp2(fmaf(s[c32 * 32 + 2 * e2], c, neg_m));
-          const float p1 = fast_exp2(fmaf(s[c32 * 32 + 2 * e2 + 1], c, neg_m));
-          rs8[(2 * e2) & 7] += p0;
-          rs8[(2 * e2 + 1) & 7] += p1;
-          pk[e2] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(p_cols + uint32_t(c32 * 16), pk);
-      }
-#pragma unroll
-      for (int w = 4; w >= 1; w >>= 1)
-#pragma unroll
-        for (int e = 0; e < w; ++e) rs8[e] += rs8[e + w];
-      l = l * alpha + rs8[0];
-      m = m_new;
-      // O correction (rare with the lazy max): O_row *= alpha once PV of tile j-1 has landed. Warp-uniform because
-      // tcgen05.ld/st are warp-wide; lanes whose max did not move scale by 1.
+      // P_j overwrites S_j; P_{j-2} V_{j-2}, the last reader of these columns, completed before s_full of tile j.
+      bool move;
+      const float alpha = softmax_step<BN, exp_poly_pairs_per8<DP>()>(lane_base + uint32_t(L::kSCol + buf * BN), j * BN, args.Skv, c,
+                                           args.rescale_thr, m, l, move);
+      // O correction (rare with the lazy max): O_row *= alpha once P_{j-1} V_{j-1} has landed.
       if (j > 0 && __any_sync(0xffffffffu, move)) {
         if (!mbar_wait_bounded(&pv_done[(j - 1) & 1], uint32_t((j - 1) >> 1) & 1u, abort_flag, args.ctl,
                                kStatusTimeoutEpilogue)) {
@@ -362,16 +491,7 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int cc = 0; cc < DP; cc += 16) {
-          uint32_t r[16];
-          tmem_ld16(lane_base + uint32_t(L::kOCol + cc), r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int t = 0; t < 16; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
-          tmem_st16(lane_base + uint32_t(L::kOCol + cc), r);
-        }
-        tmem_wait_st();
+        rescale_o_row<DP>(lane_base + uint32_t(L::kOCol), alpha);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -384,60 +504,7 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
       if (mbar_wait_bounded(&pv_done[last & 1], uint32_t(last >> 1) & 1u, abort_flag, args.ctl,
                             kStatusTimeoutEpilogue)) {
         tc_fence_after();
-        const float inv_l = 1.0f / l;
-        const int grow = q0 + row;
-        const bool store = grow < args.Sq;
-        const long long obase = (long long)bb * args.o_sb + (long long)grow * args.o_ss + (long long)hh * args.o_sh;
-#pragma unroll
-        for (int cc = 0; cc < DP; cc += 16) {
-          uint32_t r[16];
-          tmem_ld16(lane_base + uint32_t(L::kOCol + cc), r);
-          tmem_wait_ld();
-          if (store) {
-            float o[16];
-#pragma unroll
-            for (int t = 0; t < 16; ++t) o[t] = __uint_as_float(r[t]) * inv_l;
-            const int ncols = min(16, args.D - cc);
-            if (args.out_f32) {
-              float* dst = static_cast<float*>(args.out) + obase + cc;
-              if (ncols == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-#pragma unroll
-                for (int t = 0; t < 4; ++t)
-                  reinterpret_cast<float4*>(dst)[t] = make_float4(o[4 * t], o[4 * t + 1], o[4 * t + 2], o[4 * t + 3]);
-              } else {
-#pragma unroll
-                for (int t = 0; t < 16; ++t)
-                  if (t < ncols) dst[t] = o[t];
-              }
-            } else {
-              __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(args.out) + obase + cc;
-              if (ncols >= 8 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                uint4 v0;
-                v0.x = pack_bf16x2(o[0], o[1]);
-                v0.y = pack_bf16x2(o[2], o[3]);
-                v0.z = pack_bf16x2(o[4], o[5]);
-                v0.w = pack_bf16x2(o[6], o[7]);
-                reinterpret_cast<uint4*>(dst)[0] = v0;
-                if (ncols == 16) {
-                  uint4 v1;
-                  v1.x = pack_bf16x2(o[8], o[9]);
-                  v1.y = pack_bf16x2(o[10], o[11]);
-                  v1.z = pack_bf16x2(o[12], o[13]);
-                  v1.w = pack_bf16x2(o[14], o[15]);
-                  reinterpret_cast<uint4*>(dst)[1] = v1;
-                } else {
-#pragma unroll
-                  for (int t = 8; t < 16; ++t)
-                    if (t < ncols) dst[t] = __float2bfloat16_rn(o[t]);
-                }
-              } else {
-#pragma unroll
-                for (int t = 0; t < 16; ++t)
-                  if (t < ncols) dst[t] = __float2bfloat16_rn(o[t]);
-              }
-            }
-          }
-        }
+        store_o_row<DP>(lane_base + uint32_t(L::kOCol), args, q0 + warp * 32 + lane, bb, hh, 1.0f / l);
       }
     }
     tc_fence_before();
@@ -445,6 +512,248 @@ __global__ void __launch_bounds__(kAttnThreads, (AttnLayout<DP, BN, STAGES>::kSm
 
   __syncthreads();
   if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Kernel 2: two Q tiles (256 query rows) per CTA sharing every K/V tile. Warps 0-3 softmax of Q tile 0, warps 4-7
+// of Q tile 1 (warp w reaches TMEM lanes 32*(w%4)..+31), warp 8 producer, warp 9 MMA.
+// SB S buffers per Q tile (2 when 2 * (2 BN + DP) TMEM columns fit, else 1):
+//   SB = 2  MMA step t issues P_w(t-2) V then S_w(t) into the buffer P_w(t-2) occupied, for w = 0, 1. S_w(t) goes
+//           out as soon as the softmax has finished tile t-2, a whole softmax step before it is needed.
+//   SB = 1  MMA step t issues P_w(t-1) V then S_w(t): the softmax of a Q tile waits for its own P V and next S,
+//           and the other Q tile's softmax fills that gap.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kAttn2Threads = 320;
+
+template <int DP, int BN, int STAGES>
+struct Attn2Layout {
+  static constexpr int kNA = (DP + 63) / 64;
+  static constexpr int kQAtom = kAttnBM * kAtomBytesPerRow;  // 16 KB
+  static constexpr int kKVAtom = BN * kAtomBytesPerRow;
+  static constexpr int kQBytes = kNA * kQAtom;    // one Q tile
+  static constexpr int kKVBytes = kNA * kKVAtom;  // one K (or V) tile
+  static constexpr int kQOff = 0;                 // Q tile 0, then Q tile 1
+  static constexpr int kKOff = kQOff + 2 * kQBytes;
+  static constexpr int kVOff = kKOff + STAGES * kKVBytes;
+  static constexpr int kBarOff = kVOff + STAGES * kKVBytes;
+  static constexpr int SB = (2 * (2 * BN + DP) <= 512) ? 2 : 1;  // S buffers per Q tile
+  // q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2][SB], p_full[2][SB], pv_done[2], o_full[2],
+  // drain. p_full has one barrier per S buffer: with SB = 2 a softmax warpgroup may finish tiles j and j+1 before
+  // the MMA warp consumes tile j, and a single barrier would then complete two phases under one wait.
+  static constexpr int kNumBars = 1 + 4 * STAGES + 4 * SB + 4 + 1;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
+  // TMEM: S_0[0..SB) | S_1[0..SB) | O_0 | O_1. P_w(j) overwrites the first BN/2 columns of the S buffer it came from.
+  static constexpr int kSCol = 0;            // S_w[b] at (w * SB + b) * BN
+  static constexpr int kOCol = 2 * SB * BN;  // O_w at kOCol + w * DP
+  static constexpr int kTmemUsed = kOCol + 2 * DP;
+  static constexpr int kTmemCols = (kTmemUsed <= 128) ? 128 : (kTmemUsed <= 256) ? 256 : 512;
+  static_assert(DP % 16 == 0 && DP >= 16 && DP <= 192, "padded head dim must be a multiple of 16 in [16, 192]");
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 128, "key tile must be 64, 96 or 128");
+  static_assert(kTmemUsed <= 512, "S buffers + two O tiles must fit in 512 TMEM columns");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+template <int DP, int BN, int STAGES>
+__global__ void __launch_bounds__(kAttn2Threads, 1)
+    attention_fwd_qt2_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                     const __grid_constant__ CUtensorMap tm_k,
+                                     const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
+  using L = Attn2Layout<DP, BN, STAGES>;
+  constexpr int SB = L::SB;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::kQOff;
+  uint8_t* sK = smem + L::kKOff;
+  uint8_t* sV = smem + L::kVOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + STAGES;
+  uint64_t* k_empty = v_full + STAGES;
+  uint64_t* v_empty = k_empty + STAGES;
+  uint64_t* s_full = v_empty + STAGES;  // [w * SB + b]
+  uint64_t* p_full = s_full + 2 * SB;   // [w * SB + b]
+  uint64_t* pv_done = p_full + 2 * SB;
+  uint64_t* o_full = pv_done + 2;
+  uint64_t* drain = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * (2 * kAttnBM);
+  const int pair = blockIdx.y;
+  const int hh = pair % args.H;
+  const int bb = pair / args.H;
+  const int nkv = args.nkv;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int i = 0; i < 2 * SB; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], kSoftmaxWarps);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&pv_done[i], 1);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 8) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      pdl_wait();  // q/k/v may be the previous kernel's outputs
+      int c0, c1, c2, c3;
+      mbar_arrive_expect_tx(q_full, 2 * L::kQBytes);
+      for (int w = 0; w < 2; ++w)
+        for (int a = 0; a < L::kNA; ++a) {
+          map_coords(args.pq, a, q0 + w * kAttnBM, hh, bb, c0, c1, c2, c3);
+          tma_load_4d(&tm_q, q_full, sQ + w * L::kQBytes + a * L::kQAtom, c0, c1, c2, c3);
+        }
+      kv_producer<L::kNA, BN, STAGES>(&tm_k, &tm_v, args, sK, sV, k_full, v_full, k_empty, v_empty, abort_flag, hh,
+                                      bb);
+      mbar_wait_drain(q_full, 0, args.ctl);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA issuer
+    // The whole warp runs the loop (operands stay warp-uniform); one elected lane issues the MMAs and their commits.
+    bool ok = true;
+    if (args.ctl.debug & 1u) {
+      if (!mbar_wait_bounded_warp(drain, 0, abort_flag, args.ctl, kStatusForced)) ok = false;
+    }
+    if (ok && !mbar_wait_bounded_warp(q_full, 0, abort_flag, args.ctl, kStatusTimeoutMma)) ok = false;
+    tc_fence_after();
+    const uint64_t q_desc = smem_desc_kmajor_sw128(smem_u32(sQ));
+    const uint64_t k_desc = smem_desc_kmajor_sw128(smem_u32(sK));
+    const uint64_t v_desc = smem_desc_mnmajor_sw128(smem_u32(sV), L::kKVAtom);
+    // Step t, for each Q tile w: O_w += P_w(t-SB) V_{t-SB}, then S_w(t) = Q_w K_t^T into the S buffer P_w(t-SB)
+    // occupied (issued after the P V that reads it). The last SB steps only finish the P V products.
+    for (int t = 0; ok && t < nkv + SB; ++t) {
+      for (int w = 0; w < 2; ++w) {
+        if (t >= SB) {
+          const int i = t - SB;
+          const int st = i % STAGES;
+          if (w == 0 && !mbar_wait_bounded_warp(&v_full[st], uint32_t(i / STAGES) & 1u, abort_flag, args.ctl,
+                                                kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait_bounded_warp(&p_full[w * SB + i % SB], uint32_t(i / SB) & 1u, abort_flag, args.ctl,
+                                      kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (elect_one()) {
+            issue_pv<DP, BN>(tmem_base + uint32_t(L::kOCol + w * DP),
+                             tmem_base + uint32_t(L::kSCol + (w * SB + i % SB) * BN),
+                             v_desc + uint64_t((st * L::kKVBytes) >> 4), i > 0);
+            if (SB == 2) umma_commit(&pv_done[w]);
+            if (w == 1) umma_commit(&v_empty[st]);
+            if (i == nkv - 1) umma_commit(&o_full[w]);
+          }
+          __syncwarp();
+        }
+        if (t < nkv) {
+          const int st = t % STAGES;
+          if (w == 0) {
+            if (!mbar_wait_bounded_warp(&k_full[st], uint32_t(t / STAGES) & 1u, abort_flag, args.ctl,
+                                        kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          if (elect_one()) {
+            issue_s<DP, BN>(tmem_base + uint32_t(L::kSCol + (w * SB + t % SB) * BN),
+                            q_desc + uint64_t((w * L::kQBytes) >> 4), k_desc + uint64_t((st * L::kKVBytes) >> 4),
+                            L::kQAtom, L::kKVAtom);
+            umma_commit(&s_full[w * SB + t % SB]);
+            if (w == 1) umma_commit(&k_empty[st]);
+          }
+          __syncwarp();
+        }
+      }
+    }
+    if (!ok) {
+      if (elect_one()) umma_commit(drain);
+      __syncwarp();
+      mbar_wait_drain(drain, 0u, args.ctl);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / correction / epilogue (warps 0-7)
+    const int w = warp >> 2;  // Q tile
+    const int wq = warp & 3;  // TMEM lane quarter
+    const uint32_t lane_base = tmem_base + (uint32_t(wq * 32) << 16);
+    const uint32_t o_addr = lane_base + uint32_t(L::kOCol + w * DP);
+    const float c = args.scale_log2;
+    float m = -INFINITY;  // running max in log2 units (scores * scale * log2 e)
+    float l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int b = j % SB;
+      if (!mbar_wait_bounded(&s_full[w * SB + b], uint32_t(j / SB) & 1u, abort_flag, args.ctl,
+                             kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      bool move;
+      const float alpha = softmax_step<BN, exp_poly_pairs_per8<DP>()>(lane_base + uint32_t(L::kSCol + (w * SB + b) * BN), j * BN, args.Skv, c,
+                                           args.rescale_thr, m, l, move);
+      // O correction (rare with the lazy max), once P_w(j-1) V_{j-1} has landed. With one S buffer it has: it was
+      // issued before S_w(j), whose commit fired s_full.
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
+        if (SB == 2 && !mbar_wait_bounded(&pv_done[w], uint32_t(j - 1) & 1u, abort_flag, args.ctl,
+                                          kStatusTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        rescale_o_row<DP>(o_addr, alpha);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[w * SB + b]);
+    }
+    if (ok && nkv >= 1) {
+      pdl_wait();  // the previous kernel may still read the output buffer
+      if (mbar_wait_bounded(&o_full[w], 0u, abort_flag, args.ctl, kStatusTimeoutEpilogue)) {
+        tc_fence_after();
+        store_o_row<DP>(o_addr, args, q0 + w * kAttnBM + wq * 32 + lane, bb, hh, 1.0f / l);
+      }
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
   }
@@ -501,22 +810,19 @@ int encode_bshd_map(const void* base, int64_t D, int64_t S, int64_t H, int64_t B
   return kOk;
 }
 
-template <int DP, int BN, int STAGES>
-int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnArgs& a, dim3 grid,
-                cudaStream_t st, int device) {
-  using L = AttnLayout<DP, BN, STAGES>;
-  static bool configured[64] = {false};
-  auto kern = attention_fwd_tcgen05_kernel<DP, BN, STAGES>;
-  if (!configured[device]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+template <typename Kern>
+int launch_kernel(Kern kern, int smem_bytes, int threads, bool* configured, const CUtensorMap& mq,
+                  const CUtensorMap& mk, const CUtensorMap& mv, const AttnArgs& a, dim3 grid, cudaStream_t st) {
+  if (!*configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(attention smem)");
-    configured[device] = true;
+    *configured = true;
   }
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = L::kSmemBytes;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -526,40 +832,87 @@ int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, a), "attention kernel launch");
 }
 
-// Kernel variant for a padded head dim and key tile (64 or 128 keys per tile).
-int launch_for(int64_t DP, int BN, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+template <int DP, int BN, int STAGES>
+int launch_qt1(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnArgs& a, dim3 grid,
+               cudaStream_t st, int device) {
+  static bool configured[64] = {false};
+  return launch_kernel(attention_fwd_tcgen05_kernel<DP, BN, STAGES>, Attn1Layout<DP, BN, STAGES>::kSmemBytes,
+                       kAttn1Threads, &configured[device], mq, mk, mv, a, grid, st);
+}
+
+template <int DP, int BN, int STAGES>
+int launch_qt2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnArgs& a, dim3 grid,
+               cudaStream_t st, int device) {
+  static bool configured[64] = {false};
+  return launch_kernel(attention_fwd_qt2_tcgen05_kernel<DP, BN, STAGES>, Attn2Layout<DP, BN, STAGES>::kSmemBytes,
+                       kAttn2Threads, &configured[device], mq, mk, mv, a, grid, st);
+}
+
+// Kernel variant for a padded head dim, key tile and Q tiles per CTA.
+int launch_for(int64_t DP, int BN, int QT, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                const AttnArgs& a, dim3 grid, cudaStream_t st, int dev) {
-#define NPUB200_ATTN_CASE(dp, bn, stages) \
-  if (DP == dp && BN == bn) return launch_attn<dp, bn, stages>(mq, mk, mv, a, grid, st, dev);
-  // one 64-column atom of head dim (d <= 64)
-  NPUB200_ATTN_CASE(16, 64, 3)
-  NPUB200_ATTN_CASE(32, 64, 3)
-  NPUB200_ATTN_CASE(48, 64, 3)
-  NPUB200_ATTN_CASE(64, 64, 3)
-  NPUB200_ATTN_CASE(16, 128, 3)
-  NPUB200_ATTN_CASE(32, 128, 3)
-  NPUB200_ATTN_CASE(48, 128, 3)
-  NPUB200_ATTN_CASE(64, 128, 3)
-  // two atoms (64 < d <= 128)
-  NPUB200_ATTN_CASE(80, 64, 3)
-  NPUB200_ATTN_CASE(96, 64, 3)
-  NPUB200_ATTN_CASE(112, 64, 3)
-  NPUB200_ATTN_CASE(128, 64, 3)
-  NPUB200_ATTN_CASE(80, 128, 2)
-  NPUB200_ATTN_CASE(96, 128, 2)
-  NPUB200_ATTN_CASE(112, 128, 2)
-  NPUB200_ATTN_CASE(128, 128, 2)
-  // three or four atoms (128 < d <= 256): 64-key tiles only (TMEM: 2 x 64 S columns + d O columns)
-  NPUB200_ATTN_CASE(144, 64, 2)
-  NPUB200_ATTN_CASE(160, 64, 2)
-  NPUB200_ATTN_CASE(176, 64, 2)
-  NPUB200_ATTN_CASE(192, 64, 2)
-  NPUB200_ATTN_CASE(208, 64, 2)
-  NPUB200_ATTN_CASE(224, 64, 2)
-  NPUB200_ATTN_CASE(240, 64, 2)
-  NPUB200_ATTN_CASE(256, 64, 2)
-#undef NPUB200_ATTN_CASE
-  return fail(kErrUnsupported, "no attention variant for padded head dim %lld with %d-key tiles", (long long)DP, BN);
+#define NPUB200_ATTN_QT1(dp, bn, stages) \
+  if (QT == 1 && DP == dp && BN == bn) return launch_qt1<dp, bn, stages>(mq, mk, mv, a, grid, st, dev);
+#define NPUB200_ATTN_QT2(dp, bn, stages) \
+  if (QT == 2 && DP == dp && BN == bn) return launch_qt2<dp, bn, stages>(mq, mk, mv, a, grid, st, dev);
+  // One Q tile per CTA. d <= 64 with 64-key tiles: two CTAs per SM.
+  NPUB200_ATTN_QT1(16, 64, 5)
+  NPUB200_ATTN_QT1(32, 64, 5)
+  NPUB200_ATTN_QT1(48, 64, 5)
+  NPUB200_ATTN_QT1(64, 64, 5)
+  NPUB200_ATTN_QT1(16, 96, 3)
+  NPUB200_ATTN_QT1(32, 96, 3)
+  NPUB200_ATTN_QT1(48, 96, 3)
+  NPUB200_ATTN_QT1(64, 96, 3)
+  NPUB200_ATTN_QT1(16, 128, 4)
+  NPUB200_ATTN_QT1(32, 128, 4)
+  NPUB200_ATTN_QT1(48, 128, 4)
+  NPUB200_ATTN_QT1(64, 128, 4)
+  NPUB200_ATTN_QT1(80, 64, 2)
+  NPUB200_ATTN_QT1(96, 64, 2)
+  NPUB200_ATTN_QT1(112, 64, 2)
+  NPUB200_ATTN_QT1(128, 64, 2)
+  NPUB200_ATTN_QT1(80, 128, 2)
+  NPUB200_ATTN_QT1(96, 128, 2)
+  NPUB200_ATTN_QT1(112, 128, 2)
+  NPUB200_ATTN_QT1(128, 128, 2)
+  NPUB200_ATTN_QT1(144, 64, 2)
+  NPUB200_ATTN_QT1(160, 64, 2)
+  NPUB200_ATTN_QT1(176, 64, 2)
+  NPUB200_ATTN_QT1(192, 64, 2)
+  NPUB200_ATTN_QT1(208, 64, 2)
+  NPUB200_ATTN_QT1(224, 64, 2)
+  NPUB200_ATTN_QT1(240, 64, 2)
+  NPUB200_ATTN_QT1(256, 64, 2)
+  // Two Q tiles per CTA (one CTA per SM).
+  NPUB200_ATTN_QT2(16, 64, 6)
+  NPUB200_ATTN_QT2(32, 64, 6)
+  NPUB200_ATTN_QT2(48, 64, 6)
+  NPUB200_ATTN_QT2(64, 64, 6)
+  NPUB200_ATTN_QT2(16, 96, 4)
+  NPUB200_ATTN_QT2(32, 96, 4)
+  NPUB200_ATTN_QT2(48, 96, 4)
+  NPUB200_ATTN_QT2(64, 96, 4)
+  NPUB200_ATTN_QT2(16, 128, 4)
+  NPUB200_ATTN_QT2(32, 128, 4)
+  NPUB200_ATTN_QT2(48, 128, 4)
+  NPUB200_ATTN_QT2(64, 128, 4)
+  NPUB200_ATTN_QT2(80, 64, 4)
+  NPUB200_ATTN_QT2(96, 64, 4)
+  NPUB200_ATTN_QT2(112, 64, 4)
+  NPUB200_ATTN_QT2(128, 64, 4)
+  NPUB200_ATTN_QT2(80, 128, 2)
+  NPUB200_ATTN_QT2(96, 128, 2)
+  NPUB200_ATTN_QT2(112, 128, 2)
+  NPUB200_ATTN_QT2(128, 128, 2)
+  NPUB200_ATTN_QT2(144, 64, 2)
+  NPUB200_ATTN_QT2(160, 64, 2)
+  NPUB200_ATTN_QT2(176, 64, 2)
+  NPUB200_ATTN_QT2(192, 64, 2)
+#undef NPUB200_ATTN_QT1
+#undef NPUB200_ATTN_QT2
+  return fail(kErrUnsupported, "no attention variant for padded head dim %lld with %d-key tiles and %d Q tiles per CTA",
+              (long long)DP, BN, QT);
 }
 
 }  // namespace
@@ -576,13 +929,34 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   for (const void* ptr : {p.q, p.k, p.v})
     if (reinterpret_cast<uintptr_t>(ptr) & 15u) return fail(kErrInvalid, "q/k/v base addresses must be 16-byte aligned");
   const int64_t DP = (p.D + 15) / 16 * 16;
-  // Key tile (variant): for head dims up to 64 the default is 64 keys, which halves the per-CTA footprint so two
-  // CTAs share an SM (their softmax warps hide each other's latencies); 128 keys otherwise. 64 is the only tile for
-  // head dims above 128.
-  int BN = p.variant ? p.variant : (DP <= 64 ? 64 : 128);
-  if (BN != 64 && BN != 128) return fail(kErrUnsupported, "attention key tile %d (variants: 64, 128)", BN);
-  if (DP > 128) BN = 64;
+  // variant = key tile (0 = automatic, 64, 128) + 1000 * Q tiles per CTA (0 = automatic, 1, 2).
+  const int QT_req = p.variant / 1000;
+  int BN = p.variant % 1000;
+  if (p.variant < 0 || QT_req > 2 || (BN != 0 && BN != 64 && BN != 96 && BN != 128))
+    return fail(kErrUnsupported, "attention variant %d (key tile 0/64/96/128 plus 1000 x Q tiles per CTA 0/1/2)",
+                p.variant);
+  // Automatic choice (measured on the SD1.5 blocks at batch 2 and 16):
+  //   d <= 64       96-key tiles; two Q tiles per CTA once the grid of one-tile CTAs (two per SM) is at least 8 waves
+  //                 deep, one Q tile otherwise (shorter pipeline fill per CTA).
+  //   64 < d <= 128 one Q tile; 64-key tiles (two CTAs per SM) when the grid fills two per SM, else 128.
+  //   d > 128       64-key tiles; two Q tiles per CTA when one-tile CTAs would take more than one wave.
+  const int64_t ctas_qt1 = (p.Sq + kAttnBM - 1) / kAttnBM * pairs;
+  const int64_t sms = dev->sms;
+  int QT = QT_req;
+  if (DP <= 64) {
+    if (QT == 0) QT = ctas_qt1 >= 8 * 2 * sms ? 2 : 1;
+    if (BN == 0) BN = 96;
+  } else if (DP <= 128) {
+    if (QT == 0) QT = 1;
+    if (BN == 0) BN = (QT == 1 && ctas_qt1 >= 2 * sms) ? 64 : 128;
+  } else {
+    if (QT == 0) QT = (DP <= 192 && ctas_qt1 > sms) ? 2 : 1;
+    BN = 64;
+  }
+  if (QT == 2 && DP > 192) return fail(kErrUnsupported, "two Q tiles per CTA need head dim <= 192");
+  if (BN == 96 && DP > 64) BN = 64;
 
+  const int q_rows = QT * kAttnBM;
   CUtensorMap mq, mk, mv;
   AttnArgs a;
   memset(&a, 0, sizeof(a));
@@ -604,9 +978,10 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   a.ctl.status = dev->status;
   a.ctl.timeout_ns = wait_timeout_ns();
   a.ctl.debug = p.debug;
-  const dim3 grid(unsigned((p.Sq + kAttnBM - 1) / kAttnBM), unsigned(pairs));
-  if (grid.x > 0x7fffffffu) return fail(kErrInvalid, "too many query tiles");
-  return launch_for(DP, BN, mq, mk, mv, a, grid, stream, dev->device);
+  const int64_t gx = (p.Sq + q_rows - 1) / q_rows;
+  if (gx > 0x7fffffff) return fail(kErrInvalid, "too many query tiles");
+  const dim3 grid{unsigned(gx), unsigned(pairs), 1u};
+  return launch_for(DP, BN, QT, mq, mk, mv, a, grid, stream, dev->device);
 }
 
 }  // namespace npub200

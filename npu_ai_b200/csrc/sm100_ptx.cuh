@@ -118,6 +118,15 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return mbar_wait_slow(bar, parity, abort, ctl, code);
 }
 
+// Warp-wide form for roles that run their loop on all 32 lanes (an issuing warp whose MMAs go out through
+// elect_one()): every lane polls, and the verdict is the same in all lanes (false when any lane gave up; a lane
+// that gave up raised the abort flag, so the others stop within a few polls).
+__device__ __forceinline__ bool mbar_wait_bounded_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                       const KernelCtl& ctl, uint32_t code) {
+  const bool r = mbar_wait_bounded(bar, parity, abort, ctl, code);
+  return __all_sync(0xffffffffu, r);
+}
+
 // Bounded wait used only while draining after an abort: no abort check, a fixed generous deadline.
 static __device__ __noinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, const KernelCtl& ctl) {
   const uint64_t t0 = globaltimer_ns();
@@ -311,6 +320,30 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x on the FMA pipe, so a share of a softmax's exponentials leaves the MUFU (16 per clock per SM) for the
+// FP32 pipe: x = n + f with n = round(x) (adding 1.5 * 2^23 leaves round(x) in the low mantissa bits) and
+// f in [-1/2, 1/2]; 2^f = 1 + f (c1 + f (c2 + f c3)) with coefficients from a minimax fit of the relative error by
+// linear programming (fit_exp2_poly.py beside this file; max relative error 1.01e-4, a fortieth of a bf16 ulp); 2^n
+// is added into the exponent field. x is clamped at -125 so the result stays a normal float: masked keys
+// (x = -inf) give 2^-125 instead of 0, which no bf16 P or f32 row sum can see.
+__device__ __forceinline__ float exp2_poly3(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = x + 12582912.0f;
+  const float n = t - 12582912.0f;
+  const float f = x - n;
+  float p = fmaf(5.500893667e-02f, f, 2.422109544e-01f);
+  p = fmaf(p, f, 6.932829022e-01f);
+  p = fmaf(p, f, 1.0f);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {

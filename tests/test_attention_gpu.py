@@ -5,6 +5,8 @@ v ~ N(0,1), SDPA in f32 as the reference, max|err|/max|ref|, padded-stride views
 (q/k/v ~ N(0,1), scale 1/sqrt(d)), with the north star's tolerance: max-abs <= 2e-2 against SDPA in f32 on
 bf16-rounded inputs.
 """
+import functools
+
 import pytest
 import torch
 
@@ -21,6 +23,12 @@ def _qkv(B, H, Sq, Skv, D, seed=0, qk_scale=1.0):
     k = (torch.randn(B, Skv, H * D, generator=g) * qk_scale).to(torch.bfloat16)
     v = torch.randn(B, Skv, H * D, generator=g).to(torch.bfloat16)
     return q, k, v
+
+
+@functools.lru_cache(maxsize=8)
+def _block(B, H, Sq, Skv, D, seed):
+    q, k, v = _qkv(B, H, Sq, Skv, D, seed=seed)
+    return q, k, v, attention_ref(q, k, v, H)
 
 
 def _run(q, k, v, H, out_dtype=torch.float32, **kw):
@@ -41,13 +49,13 @@ def _check(o, ref, tol=TOL_ABS):
 @pytest.mark.parametrize("shape", [(2, 8, 4096, 4096, 40), (2, 8, 1024, 1024, 80), (2, 8, 256, 256, 160),
                                    (2, 8, 4096, 77, 40)],
                          ids=["self64x64_d40", "self32x32_d80", "self16x16_d160", "cross4096x77_d40"])
-@pytest.mark.parametrize("variant", [0, 64, 128])
+@pytest.mark.parametrize("variant", [0, 64, 96, 128, 1064, 1096, 1128, 2064, 2096, 2128])
 def test_baseline_blocks(cuda_device, shape, variant):
-    """the SD1.5 self-/cross-attention blocks, all (b, h) pairs in one launch, for the default
-    and both key-tile variants (64 keys: two CTAs per SM; 128 keys: one)."""
+    """The SD1.5 self-/cross-attention blocks, all (b, h) pairs in one launch, for the automatic choice and every
+    kernel variant: 64-, 96- or 128-key tiles with one query tile per CTA (two CTAs per SM where they fit) or two
+    (two S buffers per query tile where TMEM holds them)."""
     B, H, Sq, Skv, D = shape
-    q, k, v = _qkv(B, H, Sq, Skv, D, seed=D)
-    ref = attention_ref(q, k, v, H)
+    q, k, v, ref = _block(B, H, Sq, Skv, D, D)
     _check(_run(q, k, v, H, variant=variant), ref)
     _check(_run(q, k, v, H, out_dtype=torch.bfloat16, variant=variant), ref)
 
@@ -66,11 +74,22 @@ def test_reference_script_shapes(cuda_device, shape):
 @pytest.mark.parametrize("shape", [(1, 1, 1, 1, 40), (1, 2, 100, 300, 40), (3, 5, 129, 257, 80), (1, 3, 77, 77, 160),
                                    (2, 1, 300, 1, 80), (1, 2, 1000, 129, 64), (2, 2, 200, 500, 128),
                                    (1, 1, 130, 70, 24)])
-def test_ragged_shapes(cuda_device, shape):
-    """Any Sq / Skv (query and key tails handled in the kernel), odd head counts, d beyond the SD1.5 set."""
+@pytest.mark.parametrize("variant", [0, 1096, 2064, 2096, 2128])
+def test_ragged_shapes(cuda_device, shape, variant):
+    """Any Sq / Skv (query and key tails handled in the kernel), odd head counts, d beyond the SD1.5 set; also
+    forced onto the two-query-tile kernel, whose second tile is then partly or wholly past Sq."""
     B, H, Sq, Skv, D = shape
     q, k, v = _qkv(B, H, Sq, Skv, D, seed=Sq + Skv)
+    _check(_run(q, k, v, H, variant=variant), attention_ref(q, k, v, H))
+
+
+def test_head_dim_above_192_runs_one_query_tile(cuda_device):
+    """d = 256 takes the one-query-tile kernel; asking for two query tiles per CTA is refused, not faked."""
+    B, H, Sq, Skv, D = 1, 2, 300, 200, 256
+    q, k, v = _qkv(B, H, Sq, Skv, D, seed=3)
     _check(_run(q, k, v, H), attention_ref(q, k, v, H))
+    with pytest.raises(RuntimeError, match="two Q tiles"):
+        _run(q, k, v, H, variant=2064)
 
 
 def test_head_major_and_strided(cuda_device):
@@ -97,7 +116,8 @@ def test_head_major_and_strided(cuda_device):
     assert bool((out_buf[:, :, H * D:] == 5.0).all()), "kernel wrote outside the output view"
 
 
-def test_running_max_moves(cuda_device):
+@pytest.mark.parametrize("variant", [0, 1064, 1096, 2064, 2096, 2128])
+def test_running_max_moves(cuda_device, variant):
     """Later key tiles with much larger scores force the lazy running max to move (the O/l correction path)."""
     B, H, Sq, Skv, D = 1, 2, 256, 1024, 40
     g = torch.Generator().manual_seed(7)
@@ -107,7 +127,7 @@ def test_running_max_moves(cuda_device):
     k = (k * ramp).to(torch.bfloat16)
     q = (q * 2.0).to(torch.bfloat16)
     v = torch.randn(B, Skv, H * D, generator=g).to(torch.bfloat16)
-    _check(_run(q, k, v, H), attention_ref(q, k, v, H))
+    _check(_run(q, k, v, H, variant=variant), attention_ref(q, k, v, H))
 
 
 def test_custom_scale(cuda_device):
@@ -116,7 +136,8 @@ def test_custom_scale(cuda_device):
     _check(_run(q, k, v, H, scale=0.05), attention_ref(q, k, v, H, scale=0.05))
 
 
-def test_forced_timeout_reports_status_and_recovers(cuda_device):
+@pytest.mark.parametrize("variant", [1064, 2064, 2128])
+def test_forced_timeout_reports_status_and_recovers(cuda_device, variant):
     from npu_ai_b200 import kernels
     dev = torch.device("cuda", 0)
     B, H, Sq, Skv, D = 1, 2, 256, 512, 40
@@ -125,10 +146,10 @@ def test_forced_timeout_reports_status_and_recovers(cuda_device):
     kernels.set_wait_timeout_ns(2_000_000)
     kernels.set_debug_flags(1)
     try:
-        kernels.attention(q.to(dev), k.to(dev), v.to(dev), H)
+        kernels.attention(q.to(dev), k.to(dev), v.to(dev), H, variant=variant)
         with pytest.raises(RuntimeError, match="failure status"):
             kernels.check_status(dev)
     finally:
         kernels.set_debug_flags(0)
         kernels.set_wait_timeout_ns(0)
-    _check(_run(q, k, v, H), attention_ref(q, k, v, H))
+    _check(_run(q, k, v, H, variant=variant), attention_ref(q, k, v, H))
