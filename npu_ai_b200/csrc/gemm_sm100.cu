@@ -271,54 +271,59 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kIdesc = idesc_bf16_f32(kGemmBM, BN, false);
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      if (args.ctl.debug & 1u) {
-        // Test hook: wait on a barrier nothing arrives on, so the bounded wait expires and the abort path runs.
-        if (!mbar_wait_bounded(drain, 0, abort_flag, args.ctl, kStatusForced)) ok = false;
+    // The whole warp runs the loop (operands stay warp-uniform, which keeps tcgen05.mma issue at the tensor core's
+    // pace); one elected lane issues the MMAs and their commits.
+    constexpr uint32_t kIdesc = idesc_bf16_f32(kGemmBM, BN, false);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    if (args.ctl.debug & 1u) {
+      // Test hook: wait on a barrier nothing arrives on, so the bounded wait expires and the abort path runs.
+      if (!mbar_wait_bounded_warp(drain, 0, abort_flag, args.ctl, kStatusForced)) ok = false;
+    }
+    int local = 0;
+    for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_bounded_warp(&acc_empty[acc], acc_phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutMma)) {
+        ok = false;
+        break;
       }
-      int local = 0;
-      for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutMma)) {
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+      const int kb_begin = (unit % args.splits) * args.kb_per_split;
+      const int kb_end = min(num_kb, kb_begin + args.kb_per_split);
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
+        if (!mbar_wait_bounded_warp(&full[stage], phase, abort_flag, args.ctl, kStatusTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-        const int kb_begin = (unit % args.splits) * args.kb_per_split;
-        const int kb_end = min(num_kb, kb_begin + args.kb_per_split);
-        for (int kb = kb_begin; kb < kb_end; ++kb) {
-          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.ctl, kStatusTimeoutMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t a_desc = smem_desc_kmajor_sw128(smem_u32(sA + stage * L::kABytes));
-          const uint64_t b_desc = smem_desc_kmajor_sw128(smem_u32(sB + stage * L::kBBytes));
+        const uint64_t a_desc = smem_desc_kmajor_sw128(smem_u32(sA + stage * L::kABytes));
+        const uint64_t b_desc = smem_desc_kmajor_sw128(smem_u32(sB + stage * L::kBBytes));
+        if (elect_one()) {
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; ++k) {
             // +32 bytes per K step of 16 bf16 inside the swizzle atom (descriptor address field is >> 4).
             umma_f16_ss(d_tmem, a_desc + 2u * k, b_desc + 2u * k, kIdesc, (kb > kb_begin || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);  // frees the smem stage once these MMAs have read it
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
         }
-        if (!ok) break;
-        umma_commit(&acc_full[acc]);  // accumulator complete
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
-      if (!ok) {
-        // Abort: wait until every MMA this thread issued has finished before TMEM is released.
-        umma_commit(drain);
-        mbar_wait_drain(drain, 0u, args.ctl);
-      }
+      if (!ok) break;
+      if (elect_one()) umma_commit(&acc_full[acc]);  // accumulator complete
+      __syncwarp();
+    }
+    if (!ok) {
+      // Abort: wait until every MMA this warp issued has finished before TMEM is released.
+      if (elect_one()) umma_commit(drain);
+      __syncwarp();
+      mbar_wait_drain(drain, 0u, args.ctl);
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
