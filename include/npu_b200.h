@@ -78,6 +78,16 @@ int npub200_gemm_plan(int64_t m, int64_t n, int64_t k, int variant, int* tile_n_
 int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t weight, const void* bias,
                    int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace, size_t workspace_bytes,
                    int variant, void* stream);
+/* GEGLU feed-forward projection in one kernel: W is [2n, K] (nn.Linear layout of SD1.5's GEGLU `proj`: the n
+ * value rows, then the n gate rows), bias [2n] or NULL, and out[M, n] = (x.W[j] + b[j]) * gelu(x.W[n+j] + b[n+j])
+ * with the exact (erf) GELU, f32 accumulation and gating, out f32 or bf16. The reference computes the projection
+ * with NpuGemm.linear (npu/xdna1_gemm.py:428-448) and gates on the CPU in ComfyUI's GEGLU module (the "rest" of a
+ * transformer block, docs/02-results.md:411-413); here the 2n-column projection never reaches memory. `variant`:
+ * 0 or an accumulator tile in {64, 128, 192, 256} (half value, half gate columns). The workspace is used only for
+ * operands TMA cannot address; npub200_gemm_workspace_size() with 2n columns gives a sufficient size. */
+int npub200_gemm_geglu(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                       const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace,
+                       size_t workspace_bytes, int variant, void* stream);
 
 /* ----------------------------------------------------------------------------------------------------------
  * GEMM without a workspace, for callers that cannot allocate device memory (a host whose device memory is owned

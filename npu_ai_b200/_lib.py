@@ -31,6 +31,8 @@ _SIGNATURES = {
                                          ctypes.POINTER(ctypes.c_int)]),
     "npub200_gemm": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p, ctypes.c_int, _c_p,
                                     _c_i64, ctypes.c_int, _c_p, ctypes.c_size_t, ctypes.c_int, _c_p]),
+    "npub200_gemm_geglu": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p, ctypes.c_int,
+                                          _c_p, _c_i64, ctypes.c_int, _c_p, ctypes.c_size_t, ctypes.c_int, _c_p]),
     "npub200_gemm_noalloc": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p, ctypes.c_int,
                                             _c_p, _c_i64, ctypes.c_int, ctypes.c_int, _c_p]),
     "npub200_gemm_w": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, ctypes.c_int, _c_p, _c_i64,

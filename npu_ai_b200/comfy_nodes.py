@@ -122,6 +122,7 @@ class B200Runtime:
         self.gemm = NpuGemm(device=device, verbose=False)
         self.weights: dict[int, tuple] = {}      # id(module) -> (NpuWeight, bias tensor | None, name)
         self.installed: dict[int, tuple] = {}    # id(module) -> (module, original forward)
+        self.geglu_modules: set[int] = set()     # GEGLU modules routed to the fused projection + gating kernel
         self.enabled = False
         self.record_only = False
         self.recorded: set[tuple[int, int, int]] = set()
@@ -145,6 +146,14 @@ class B200Runtime:
             self.installed[id(mod)] = (mod, mod.forward)
             mod.forward = types.MethodType(_gpu_linear_forward, mod)
             n_new += 1
+        # GEGLU feed-forward blocks whose projection was taken over: projection + gating in one kernel.
+        for name, mod in diffusion_model.named_modules():
+            proj = getattr(mod, "proj", None)
+            if (type(mod).__name__ == "GEGLU" and isinstance(proj, torch.nn.Linear) and id(proj) in self.weights
+                    and id(mod) not in self.installed and proj.out_features % 2 == 0):
+                self.installed[id(mod)] = (mod, mod.forward)
+                self.geglu_modules.add(id(mod))
+                mod.forward = types.MethodType(_gpu_geglu_forward, mod)
         return n_new
 
     def release(self) -> None:
@@ -154,6 +163,7 @@ class B200Runtime:
             w.release()
         self.installed.clear()
         self.weights.clear()
+        self.geglu_modules.clear()
         self.enabled = False
 
 
@@ -170,6 +180,26 @@ def _gpu_linear_forward(self: torch.nn.Linear, x: torch.Tensor) -> torch.Tensor:
         return torch.nn.functional.linear(x, self.weight, self.bias)
     out_dtype = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
     y = rt.gemm.linear(x, w, bias, out_dtype=out_dtype)
+    return y if y.dtype == x.dtype else y.to(dtype=x.dtype)
+
+
+def _gpu_geglu_forward(self, x: torch.Tensor) -> torch.Tensor:
+    """GEGLU.forward (`a, gate = proj(x).chunk(2, -1); a * gelu(gate)`) as one GEMM whose epilogue gates: the
+    2n-wide projection never reaches memory. Falls back to the module's own forward exactly where its Linear
+    would (runtime off, discovery pass, too few tokens, CPU tensors)."""
+    rt = _RUNTIME
+    proj = self.proj
+    entry = rt.weights.get(id(proj)) if rt is not None else None
+    tokens = x.numel() // x.shape[-1] if x.numel() else 0
+    if (entry is None or not rt.enabled or rt.record_only or tokens < rt.min_tokens or x.device.type != "cuda"
+            or id(self) not in rt.installed):
+        if rt is not None and id(self) in rt.installed:
+            return rt.installed[id(self)][1](x)
+        a, gate = proj(x).chunk(2, dim=-1)
+        return a * torch.nn.functional.gelu(gate)
+    w, bias, _name = entry
+    out_dtype = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
+    y = rt.gemm.linear_geglu(x, w, bias, out_dtype=out_dtype)
     return y if y.dtype == x.dtype else y.to(dtype=x.dtype)
 
 
@@ -368,8 +398,8 @@ class B200Status:
         if rt is None:
             s = "B200 runtime not started"
         else:
-            s = (rt.gemm.summary() + " | layers on GPU kernels: %d | %s | last: %s"
-                 % (len(rt.weights), rt.attn.summary(), rt.last_summary))
+            s = (rt.gemm.summary() + " | layers on GPU kernels: %d (GEGLU blocks fused: %d) | %s | last: %s"
+                 % (len(rt.weights), len(rt.geglu_modules), rt.attn.summary(), rt.last_summary))
         _log(s)
         return {"ui": {"text": [s]}, "result": (s,)}
 

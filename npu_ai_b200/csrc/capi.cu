@@ -124,11 +124,12 @@ struct WsLayout {
 };
 
 WsLayout gemm_ws_layout(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
-                        int variant, int sms) {
+                        int variant, int sms, int geglu = 0) {
   WsLayout L;
   const int64_t kp = round_up(k, 8);
   const bool pad_k = (k % 8) != 0;
-  L.split_bytes = sms > 0 ? gemm_plan(m, n, kp, sms, variant).split_ws_bytes : 0;  // counters + partials
+  const int64_t w_rows = geglu ? 2 * n : n;
+  L.split_bytes = (sms > 0 && !geglu) ? gemm_plan(m, n, kp, sms, variant).split_ws_bytes : 0;  // counters + partials
   size_t off = L.split_bytes > 0 ? L.split_bytes : kCounterRegion;
   if (pad_k || !tma_rows_ok(x, ldx, k)) {
     L.x_off = off;
@@ -137,7 +138,7 @@ WsLayout gemm_ws_layout(const void* x, int64_t ldx, int64_t m, int64_t k, const 
   }
   if (w != nullptr && (pad_k || !tma_rows_ok(w, ldw, k))) {
     L.w_off = off;
-    L.w_bytes = size_t(round_up(n * kp * 2, 256));
+    L.w_bytes = size_t(round_up(w_rows * kp * 2, 256));
     off += L.w_bytes;
   }
   L.total = (L.split_bytes > 0 || L.x_bytes > 0 || L.w_bytes > 0) ? off : 0;
@@ -163,13 +164,14 @@ int check_gemm_common(int64_t m, int64_t k, int64_t n, int bias_dtype, const voi
 namespace npub200 {
 
 size_t gemm_workspace_bytes(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
-                            int variant, int sms) {
-  return gemm_ws_layout(x, ldx, m, k, w, ldw, n, variant, sms).total;
+                            int variant, int sms, int geglu) {
+  return gemm_ws_layout(x, ldx, m, k, w, ldw, n, variant, sms, geglu).total;
 }
 
 int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
                         const CUtensorMap* w_map, const void* bias, int bias_dtype, void* out, int64_t ldo,
-                        int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream) {
+                        int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream,
+                        int geglu) {
   if (int rc = check_gemm_common(m, k, n, bias_dtype, out, ldo, out_dtype)) return rc;
   if (x == nullptr || w == nullptr) return fail(kErrInvalid, "GEMM operand pointer is null");
   if (ldx < k) return fail(kErrInvalid, "x row stride %lld < K=%lld", (long long)ldx, (long long)k);
@@ -192,13 +194,14 @@ int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const 
   p.variant = variant;
   p.w_map_cache = w_map;
   p.debug = g_debug_flags.load();
+  p.geglu = geglu;
 
   const DeviceInfo* dev = nullptr;
   if (int rc = current_device_info(&dev)) return rc;
   const bool pad_k = (k % 8) != 0;
   const bool x_ok = !pad_k && tma_rows_ok(x, ldx, k);
   const bool w_ok = !pad_k && tma_rows_ok(w, ldw, k);
-  const WsLayout L = gemm_ws_layout(x, ldx, m, k, w_map ? nullptr : w, ldw, n, variant, dev->sms);
+  const WsLayout L = gemm_ws_layout(x, ldx, m, k, w_map ? nullptr : w, ldw, n, variant, dev->sms, geglu);
   if (workspace != nullptr && !aligned16(workspace)) return fail(kErrInvalid, "workspace must be 16-byte aligned");
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const int64_t kp = round_up(k, 8);
@@ -213,7 +216,7 @@ int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const 
       p.ldx = kp;
     }
     if (!w_ok) {
-      if (int rc = repack_rows_bf16(w, ldw, n, k, ws + L.w_off, kp, st)) return rc;
+      if (int rc = repack_rows_bf16(w, ldw, geglu ? 2 * n : n, k, ws + L.w_off, kp, st)) return rc;
       p.w = ws + L.w_off;
       p.ldw = kp;
       p.w_map_cache = nullptr;
@@ -309,6 +312,15 @@ int npub200_gemm(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w
   if (int rc = check_gemm_common(m, k, n, bias_dtype, out, ldo, out_dtype)) return rc;
   return gemm_common(x, ldx, m, k, w, ldw, n, nullptr, bias, bias_dtype, out, ldo, out_dtype, workspace,
                      workspace_bytes, variant, stream);
+}
+
+int npub200_gemm_geglu(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                       const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace,
+                       size_t workspace_bytes, int variant, void* stream) {
+  if (int rc = check_gemm_common(m, k, n, bias_dtype, out, ldo, out_dtype)) return rc;
+  if (n > INT32_MAX / 4) return fail(kErrInvalid, "GEGLU width %lld too large", (long long)n);
+  return gemm_with_workspace(x, ldx, m, k, w, ldw, n, nullptr, bias, bias_dtype, out, ldo, out_dtype, workspace,
+                             workspace_bytes, variant, stream, 1);
 }
 
 int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t weight, const void* bias,

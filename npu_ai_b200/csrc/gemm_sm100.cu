@@ -11,7 +11,11 @@
 //               TMEM, double-buffered so the epilogue of tile i overlaps the main loop of tile i+1
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator rows, bias add, cast, predicated stores
 // Ragged M/N/K need no padding: TMA zero-fills out-of-bounds rows and columns, the epilogue stores only rows < M
-// and columns < N. The only layout requirement is TMA's: 16-byte aligned base and row strides (K % 8 == 0 for a
+// and columns < N.
+// GEGLU form (template flag): W holds 2N rows ([a; gate], the GEGLU projection of SD1.5's feed-forward block) and
+// out[:, j] = (x.W[j] + b[j]) * gelu(x.W[N+j] + b[N+j]), the exact (erf) GELU. A tile's BN accumulator columns are
+// BN/2 a-rows and the BN/2 matching gate rows (two TMA boxes per stage), so the epilogue gates in registers and
+// the 2N-column projection is never written to memory. The only layout requirement is TMA's: 16-byte aligned base and row strides (K % 8 == 0 for a
 // dense matrix); anything else is repacked by the host into a caller-provided workspace first.
 #include <algorithm>
 #include <cstdio>
@@ -31,6 +35,7 @@ struct GemmArgs {
   int n_fastest;  // tile raster: 1 = N tiles innermost (x stays in L2 across them), 0 = M tiles innermost
   const void* bias;
   int bias_f32;
+  int bias_n;     // bias entries (N, or 2N in the GEGLU form)
   void* out;
   long long ldo;
   int out_f32;
@@ -72,7 +77,7 @@ __device__ __forceinline__ void load_bias32(const GemmArgs& a, int gcol, float (
   }
   if (a.bias_f32) {
     const float* p = static_cast<const float*>(a.bias) + gcol;
-    if (gcol + 32 <= a.N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    if (gcol + 32 <= a.bias_n && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float4 t = __ldg(reinterpret_cast<const float4*>(p) + j);
@@ -83,11 +88,11 @@ __device__ __forceinline__ void load_bias32(const GemmArgs& a, int gcol, float (
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) b[j] = (gcol + j < a.N) ? __ldg(p + j) : 0.0f;
+      for (int j = 0; j < 32; ++j) b[j] = (gcol + j < a.bias_n) ? __ldg(p + j) : 0.0f;
     }
   } else {
     const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(a.bias) + gcol;
-    if (gcol + 32 <= a.N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    if (gcol + 32 <= a.bias_n && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint4 t = __ldg(reinterpret_cast<const uint4*>(p) + j);
@@ -100,7 +105,7 @@ __device__ __forceinline__ void load_bias32(const GemmArgs& a, int gcol, float (
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) b[j] = (gcol + j < a.N) ? __bfloat162float(p[j]) : 0.0f;
+      for (int j = 0; j < 32; ++j) b[j] = (gcol + j < a.bias_n) ? __bfloat162float(p[j]) : 0.0f;
     }
   }
 }
@@ -141,6 +146,9 @@ __device__ __forceinline__ void store_row32_direct(const GemmArgs& a, int grow, 
   }
 }
 
+// GELU with the error function (torch's default `F.gelu`, approximate='none').
+__device__ __forceinline__ float gelu_erf(float y) { return 0.5f * y * (1.0f + erff(y * 0.70710678118654752f)); }
+
 __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& m_blk, int& n_blk) {
   if (a.n_fastest) {
     m_blk = tile / a.num_n_blk;
@@ -151,11 +159,23 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& m_
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool GEGLU>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                              const __grid_constant__ CUtensorMap tm_out, const GemmArgs args) {
   using L = GemmLayout<BN, STAGES>;
+  // Output columns per tile: BN, or BN/2 gated columns in the GEGLU form (a then gate rows of W in the B tile).
+  constexpr int kOutCols = GEGLU ? BN / 2 : BN;
+  static_assert(!GEGLU || (BN % 64 == 0), "GEGLU tiles hold two halves of a multiple of 32 columns");
+  // W tile of stage i for the output-column block nb: one box of BN rows, or BN/2 a-rows then BN/2 gate-rows.
+  auto load_w = [&](uint64_t* bar, uint8_t* dst, int kb, int nb) {
+    if constexpr (GEGLU) {
+      tma_load_2d(&tm_w, bar, dst, kb * kGemmBK, nb * kOutCols);
+      tma_load_2d(&tm_w, bar, dst + kOutCols * 128, kb * kGemmBK, args.N + nb * kOutCols);
+    } else {
+      tma_load_2d(&tm_w, bar, dst, kb * kGemmBK, nb * BN);
+    }
+  };
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -221,7 +241,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         pre = min(STAGES, min(num_kb, kb0 + args.kb_per_split) - kb0);
         for (int i = 0; i < pre; ++i) {
           mbar_arrive_expect_tx(&full[i], L::kStageBytes);
-          tma_load_2d(&tm_w, &full[i], sB + i * L::kBBytes, (kb0 + i) * kGemmBK, nb * BN);
+          load_w(&full[i], sB + i * L::kBBytes, kb0 + i, nb);
         }
       }
       pdl_wait();  // x may be the previous kernel's output
@@ -230,7 +250,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int mb, nb;
         tile_coords(args, tile, mb, nb);
         const int m0 = mb * kGemmBM;
-        const int n0 = nb * BN;
         const int kb_begin = (unit % args.splits) * args.kb_per_split;
         const int kb_end = min(num_kb, kb_begin + args.kb_per_split);
         for (int kb = kb_begin; kb < kb_end; ++kb) {
@@ -245,7 +264,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
             tma_load_2d(&tm_x, &full[stage], sA + stage * L::kABytes, kb * kGemmBK, m0);
-            tma_load_2d(&tm_w, &full[stage], sB + stage * L::kBBytes, kb * kGemmBK, n0);
+            load_w(&full[stage], sB + stage * L::kBBytes, kb, nb);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -347,9 +366,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int pmb, pnb;
         tile_coords(args, unit / splits, pmb, pnb);
         const int esz = args.bias_f32 ? 4 : 2;
-        const int bytes = min(BN, args.N - pnb * BN) * esz;
+        const int bytes = min(kOutCols, args.N - pnb * kOutCols) * esz;
         if (lane * 128 < bytes)
-          prefetch_l2(static_cast<const uint8_t*>(args.bias) + size_t(pnb) * BN * esz + lane * 128);
+          prefetch_l2(static_cast<const uint8_t*>(args.bias) + size_t(pnb) * kOutCols * esz + lane * 128);
+        if (GEGLU && lane * 128 < bytes)
+          prefetch_l2(static_cast<const uint8_t*>(args.bias) + (size_t(args.N) + size_t(pnb) * kOutCols) * esz +
+                      lane * 128);
       }
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.ctl, kStatusTimeoutEpilogue)) break;
       tc_fence_after();
@@ -358,10 +380,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int mb, nb;
       tile_coords(args, tile, mb, nb);
       const int m0 = mb * kGemmBM;
-      const int n0 = nb * BN;
+      const int n0 = nb * kOutCols;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
       bool emit = true;
-      if (splits > 1) {
+      if (!GEGLU && splits > 1) {
         // Publish this split's partial, then take a ticket; the last split of the tile reduces.
         float* mine = args.ws_partial + (size_t(tile) * splits + split) * BN * kGemmBM;
 #pragma unroll 1
@@ -384,40 +406,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (emit) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += cw) {
-          const bool chunk_tma = args.tma_store && c0 + cw <= BN;
+        for (int c0 = 0; c0 < kOutCols; c0 += cw) {
+          const bool chunk_tma = args.tma_store && c0 + cw <= kOutCols;
           uint8_t* sb = staging + (chunk_no & 1) * (32 * 128);
           if (chunk_tma) {
             if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
             __syncwarp();
           }
 #pragma unroll 1
-          for (int c = c0; c < min(c0 + cw, BN); c += 32) {
+          for (int c = c0; c < min(c0 + cw, kOutCols); c += 32) {
             uint32_t r[32];
             tmem_ld32(t_row + uint32_t(c), r);
             float b[32];
             load_bias32(args, n0 + c, b);
-            tmem_wait_ld();
             float v[32];
-            if (splits > 1) {
-              // Fixed summation order over the splits, this split's own partial taken from TMEM.
+            if constexpr (GEGLU) {
+              uint32_t rg[32];
+              tmem_ld32(t_row + uint32_t(kOutCols + c), rg);
+              float bg[32];
+              load_bias32(args, args.N + n0 + c, bg);
+              tmem_wait_ld();
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = 0.0f;
-              for (int sp = 0; sp < splits; ++sp) {
-                if (sp == split) {
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r[j]);
-                } else {
-                  const float* part = args.ws_partial + (size_t(tile) * splits + sp) * BN * kGemmBM;
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) v[j] += __ldcg(part + (c + j) * kGemmBM + row);
-                }
-              }
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += b[j];
+              for (int j = 0; j < 32; ++j)
+                v[j] = (__uint_as_float(r[j]) + b[j]) * gelu_erf(__uint_as_float(rg[j]) + bg[j]);
             } else {
+              tmem_wait_ld();
+              if (splits > 1) {
+                // Fixed summation order over the splits, this split's own partial taken from TMEM.
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + b[j];
+                for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+                for (int sp = 0; sp < splits; ++sp) {
+                  if (sp == split) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r[j]);
+                  } else {
+                    const float* part = args.ws_partial + (size_t(tile) * splits + sp) * BN * kGemmBM;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] += __ldcg(part + (c + j) * kGemmBM + row);
+                  }
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += b[j];
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + b[j];
+              }
             }
             if (chunk_tma) {
               uint8_t* rowp = sb + lane * 128;
@@ -455,7 +488,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ++chunk_no;
           }
         }
-        if (splits > 1 && threadIdx.x == 64) args.ws_counter[tile] = 0u;  // leave the counter zeroed for reuse
+        if (!GEGLU && splits > 1 && threadIdx.x == 64) args.ws_counter[tile] = 0u;  // leave the counter zeroed for reuse
       }
       tc_fence_before();
       __syncwarp();
@@ -476,12 +509,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ---------------------------------------------------------------------------------------------------------------
 namespace {
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool GEGLU = false>
 int launch_variant(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mo, const GemmArgs& args,
                    int grid, cudaStream_t st, int device) {
   using L = GemmLayout<BN, STAGES>;
   static bool configured[64] = {false};
-  auto kern = gemm_bf16_tcgen05_kernel<BN, STAGES>;
+  auto kern = gemm_bf16_tcgen05_kernel<BN, STAGES, GEGLU>;
   if (device < 0 || device >= 64) return fail(kErrInvalid, "device ordinal %d out of range", device);
   if (!configured[device]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
@@ -559,16 +592,20 @@ double plan_cost(int64_t M, int64_t N, int64_t kb, int bn, int splits, int sms) 
 }
 }  // namespace
 
-GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant) {
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool geglu) {
+  // N counts accumulator columns: for the GEGLU form the 2 x inner projection columns, and only tiles with an even
+  // split into a and gate halves of 32-column multiples are candidates.
   const int64_t kb = (K + kGemmBK - 1) / kGemmBK;
   GemmPlan best{128, 1, int(kb), 0};
   double best_cost = 1e300;
   for (int bn : kTileChoices) {
     if (variant && bn != variant) continue;
+    if (geglu && bn % 64 != 0) continue;
     const int64_t tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + bn - 1) / bn);
-    // Split K only when the tiles leave most SMs idle and each split keeps >= 4 K blocks.
+    // Split K only when the tiles leave most SMs idle and each split keeps >= 4 K blocks (never for GEGLU, whose
+    // gating needs the finished sums).
     int max_split = 1;
-    if (tiles * 2 <= sms && tiles * 4 <= int64_t(kSplitCounterBytes) && kb >= 8) max_split = int(std::min<int64_t>(std::min<int64_t>(sms / tiles, kb / 4), 16));
+    if (!geglu && tiles * 2 <= sms && tiles * 4 <= int64_t(kSplitCounterBytes) && kb >= 8) max_split = int(std::min<int64_t>(std::min<int64_t>(sms / tiles, kb / 4), 16));
     for (int sp = 1; sp <= max_split; ++sp) {
       const int kps = int((kb + sp - 1) / sp);
       const int eff = int((kb + kps - 1) / kps);  // splits actually needed with kps blocks each
@@ -597,13 +634,17 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
                                                     (long long)p.M, (long long)p.N, (long long)p.K);
   if (p.M > INT32_MAX / 2 || p.N > INT32_MAX / 2 || p.K > INT32_MAX / 2)
     return fail(kErrInvalid, "GEMM dimension too large");
+  const bool geglu = p.geglu != 0;
   if (p.variant) {
     bool known = false;
-    for (int c : kTileChoices) known |= (c == p.variant);
-    if (!known) return fail(kErrUnsupported, "no GEMM variant with an N tile of %d", p.variant);
+    for (int c : kTileChoices) known |= (c == p.variant) && (!geglu || c % 64 == 0);
+    if (!known)
+      return fail(kErrUnsupported, "no GEMM%s variant with an N tile of %d", geglu ? " (GEGLU)" : "", p.variant);
   }
-  GemmPlan plan = gemm_plan(p.M, p.N, p.K, dev->sms, p.variant);
+  if (geglu && p.w_map_cache != nullptr) return fail(kErrInvalid, "the GEGLU form encodes its own weight map");
+  GemmPlan plan = gemm_plan(p.M, geglu ? 2 * p.N : p.N, p.K, dev->sms, p.variant, geglu);
   const int bn = plan.bn;
+  const int out_cols = geglu ? bn / 2 : bn;  // output columns per tile
   if (plan.splits > 1 && (p.ws_split == nullptr || p.ws_split_bytes < plan.split_ws_bytes ||
                           (reinterpret_cast<uintptr_t>(p.ws_split) & 255) != 0)) {
     plan.splits = 1;  // no room for partials: one CTA per tile over all of K
@@ -614,7 +655,7 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   if (int rc = encode_kmajor_map(p.x, p.M, p.K, p.ldx, kGemmBM, &mx)) return rc;
   if (p.w_map_cache != nullptr) {
     mw = *p.w_map_cache;
-  } else if (int rc = encode_kmajor_map(p.w, p.N, p.K, p.ldw, bn, &mw)) {
+  } else if (int rc = encode_kmajor_map(p.w, geglu ? 2 * p.N : p.N, p.K, p.ldw, geglu ? bn / 2 : bn, &mw)) {
     return rc;
   }
 
@@ -631,7 +672,7 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.N = int(p.N);
   a.K = int(p.K);
   a.num_m_blk = int((p.M + kGemmBM - 1) / kGemmBM);
-  const int num_n = int((p.N + bn - 1) / bn);
+  const int num_n = int((p.N + out_cols - 1) / out_cols);
   a.num_n_blk = num_n;
   // Raster: keep the larger operand's tiles in L2 while the smaller one streams past them.
   a.n_fastest = (p.M >= p.N) ? 1 : 0;
@@ -641,6 +682,7 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.num_kb = int((p.K + kGemmBK - 1) / kGemmBK);
   a.bias = p.bias;
   a.bias_f32 = p.bias_f32;
+  a.bias_n = int(geglu ? 2 * p.N : p.N);
   a.out = p.out;
   a.ldo = p.ldo;
   a.out_f32 = p.out_f32;
@@ -654,6 +696,15 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.ctl.debug = p.debug;
   const int grid = int(std::min<int64_t>(tiles * plan.splits, dev->sms));
 
+  if (geglu) {
+    switch (bn) {
+      case 64: return launch_variant<64, 8, true>(mx, mw, mo, a, grid, stream, dev->device);
+      case 128: return launch_variant<128, 6, true>(mx, mw, mo, a, grid, stream, dev->device);
+      case 192: return launch_variant<192, 4, true>(mx, mw, mo, a, grid, stream, dev->device);
+      case 256: return launch_variant<256, 4, true>(mx, mw, mo, a, grid, stream, dev->device);
+    }
+    return fail(kErrUnsupported, "no GEGLU GEMM variant with an N tile of %d", bn);
+  }
   switch (bn) {
     case 64: return launch_variant<64, 8>(mx, mw, mo, a, grid, stream, dev->device);
     case 96: return launch_variant<96, 6>(mx, mw, mo, a, grid, stream, dev->device);

@@ -58,6 +58,7 @@ struct GemmProblem {
   void* ws_split;                  // split-K workspace: zeroed counters, then f32 partials (may be null)
   size_t ws_split_bytes;
   uint32_t debug;
+  int geglu;  // 1: W has 2N rows [a; gate] and out[:, j] = (x.W[j] + b[j]) * gelu(x.W[N+j] + b[N+j]); bias has 2N
 };
 // Launch plan for a problem: the N tile and the split-K factor (what `variant == 0` resolves to).
 struct GemmPlan {
@@ -66,15 +67,16 @@ struct GemmPlan {
   int kb_per_split;
   size_t split_ws_bytes;  // bytes of split-K workspace the plan needs (0 when splits == 1)
 };
-GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant);
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool geglu = false);
 int gemm_encode_b_map(const void* w, int64_t ldw, int64_t N, int64_t K, int bn, CUtensorMap* out);
 // Bytes of workspace the GEMM entry points use for a problem (split-K counters + partials, repack buffers).
 size_t gemm_workspace_bytes(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
-                            int variant, int sms);
+                            int variant, int sms, int geglu = 0);
 // The GEMM entry point's body with a caller-given workspace (argument checks, repacking, split-K, launch).
 int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
                         const CUtensorMap* w_map, const void* bias, int bias_dtype, void* out, int64_t ldo,
-                        int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream);
+                        int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream,
+                        int geglu = 0);
 int gemm_launch(const GemmProblem& p, cudaStream_t stream);
 // bf16 copy of a row-strided matrix into a dense [rows, cols_pad] buffer, zero-filling the pad columns.
 int repack_rows_bf16(const void* src, int64_t ld_src, int64_t rows, int64_t cols, void* dst, int64_t cols_pad,

@@ -121,6 +121,44 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out
     return out
 
 
+def gemm_geglu(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+               out_dtype: torch.dtype = torch.float32, variant: int = 0) -> torch.Tensor:
+    """GEGLU projection in one kernel: with y = x @ w^T (+ bias), out[M, n] = y[:, :n] * gelu(y[:, n:]).
+
+    w is the [2n, K] bf16 weight of the GEGLU `proj` Linear (value rows, then gate rows), bias bf16/f32 [2n];
+    f32 accumulation and gating, exact (erf) GELU. The 2n-wide projection is never written to memory.
+    """
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("gemm_geglu operands must be bf16")
+    if x.dim() != 2 or w.dim() != 2 or x.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("gemm_geglu operands must be 2-D with contiguous rows")
+    M, K = x.shape
+    N2, K2 = w.shape
+    if K != K2:
+        raise AssertionError(f"K mismatch: x has {K}, weight has {K2}")
+    if N2 % 2:
+        raise ValueError(f"GEGLU weight needs an even number of rows (value and gate halves), got {N2}")
+    n = N2 // 2
+    if out is None:
+        out = torch.empty((M, n), dtype=out_dtype, device=x.device)
+    if out.dtype not in _DT or out.stride(1) != 1 or tuple(out.shape) != (M, n):
+        raise ValueError("out must be an [M, n] bf16/f32 matrix with contiguous rows")
+    if bias is not None:
+        if bias.dtype not in _DT or bias.numel() != N2 or not bias.is_contiguous():
+            raise ValueError("bias must be a contiguous [2n] bf16/f32 vector")
+    ws = _gemm_workspace(x, w, M, K, N2, variant)  # sized for the 2n-row weight: covers every repack
+    with torch.cuda.device(x.device):
+        _lib.call("npub200_gemm_geglu", ctypes.c_void_p(x.data_ptr()), x.stride(0), M, K,
+                  ctypes.c_void_p(w.data_ptr()), w.stride(0), n,
+                  ctypes.c_void_p(bias.data_ptr()) if bias is not None else None,
+                  _DT[bias.dtype] if bias is not None else _lib.DTYPE_BF16,
+                  ctypes.c_void_p(out.data_ptr()), out.stride(0), _DT[out.dtype],
+                  ctypes.c_void_p(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
+                  int(variant), ctypes.c_void_p(_stream_ptr(x.device)))
+    return out
+
+
 def _bshd_strides(t: torch.Tensor, head_major: bool) -> tuple[int, int, int]:
     """(batch, seq, head) element strides of a (B, S, H, D) view given as (B, S, H*D) or (B, H, S, D)."""
     if head_major:

@@ -289,6 +289,27 @@ class NpuGemm:
         y = self.matmul_t(x2, w, bias, out_dtype=out_dtype).view(*shp[:-1], w.N)
         return y if is_torch else y.cpu().numpy()
 
+    def linear_geglu(self, x, w: NpuWeight, bias=None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        """GEGLU feed-forward projection in one kernel: x (..., K) with w the resident [2n, K] weight of a GEGLU
+        `proj` Linear -> (..., n) = y[..., :n] * gelu(y[..., n:]), y = x @ W^T (+ bias). The reference offloads the
+        projection through linear() (npu/xdna1_gemm.py:428-448) and gates on the host."""
+        t_start = time.perf_counter()
+        xt = _as_tensor(x)
+        shp = tuple(xt.shape)
+        x2 = self._x_device(xt.reshape(-1, shp[-1]))
+        M, K = x2.shape
+        assert K == w.K, f"K mismatch: x has {K}, weight has {w.K}"
+        ev = self._events()
+        y = kernels.gemm_geglu(x2, w.tensor[:, :K] if w.tensor.shape[1] != K else w.tensor, self._bias_device(bias),
+                               out_dtype=out_dtype or self.out_dtype)
+        self._close("gemm", ev)
+        with self._lock:
+            self.stats["calls"] += 1
+            self.stats["dispatches"] += 1
+            self.stats["flops"] += 2.0 * M * K * w.N
+            self.stats["total_seconds"] += time.perf_counter() - t_start
+        return y.view(*shp[:-1], w.N // 2)
+
     # -- attention ------------------------------------------------------------------------------
     def attention_fused_fits(self, tq: int, tk: int, d: int, bh: int) -> bool:
         return d % 8 == 0 and 8 <= d <= 256 and tq >= 1 and tk >= 1 and 1 <= bh <= 65535

@@ -10,11 +10,14 @@ checks its NPU results against.
     `F.linear`, comfyui/custom_nodes/comfyui_xdna1_npu/__init__.py:151), bias added in f32 after the product
     (npu/xdna1_gemm.py:417-418).
   * Attention: scaled dot-product attention in f32 on bf16-rounded q/k/v (scripts/11-attn-fused-test.py:115-119).
-  * aie_numerics: a numpy restatement of the AIE kernel's own arithmetic (npu/kernels/xdna1_attn.cc) used to
-    show how far the reference's NPU numerics sit from the f32 oracle.
+  * GEGLU feed-forward projection: the projection as above, then value * gelu(gate) in f32 with the exact (erf)
+    GELU, as the host side of a transformer block computes it after the reference's Linear offload
+    (docs/02-results.md:411-413 lists GEGLU among the host work; ComfyUI's GEGLU module is
+    `x, gate = proj(x).chunk(2, dim=-1); return x * F.gelu(gate)`).
 Pinning: tests/golden/ holds fixtures produced by running the reference's CPU fallback code itself
 (tests/golden/make_golden.py imports the reference's ComfyUI node module) and the reference's published
 accuracy figures (docs/02-results.md:709) that the attention oracle reproduces on the reference's own seeded
 inputs; see tests/test_oracle.py.
 """
-from .reference_ops import attention_ref, bf16_round, cosine, linear_ref, rel_l2_err, rel_max_err  # noqa: F401
+from .reference_ops import (attention_ref, bf16_round, cosine, geglu_ref, linear_ref, rel_l2_err,  # noqa: F401
+                            rel_max_err)

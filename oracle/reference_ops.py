@@ -26,6 +26,15 @@ def linear_ref(x: torch.Tensor, w_nk: torch.Tensor, bias: torch.Tensor | None = 
     return y.reshape(*x.shape[:-1], w_nk.shape[0])
 
 
+def geglu_ref(x: torch.Tensor, w_2n_k: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """f32 GEGLU: y = linear_ref(x, W, bias) over the 2n rows of W (value rows, then gate rows), then
+    y[..., :n] * gelu(y[..., n:]) with the exact (erf) GELU, the host-side rest of SD1.5's feed-forward block after
+    the reference offloads its Linear (docs/02-results.md:411-413)."""
+    y = linear_ref(x, w_2n_k, bias)
+    a, gate = y.chunk(2, dim=-1)
+    return a * F.gelu(gate)
+
+
 def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
                   head_major: bool = False) -> torch.Tensor:
     """f32 softmax(bf16(q) bf16(k)^T * scale) bf16(v) for every (batch, head) pair.

@@ -75,17 +75,20 @@ def test_offload_node_end_to_end(cuda_device, unet_pair):
         y2 = patched.apply_model(x, t, ctx).float()
     rt = cn._RUNTIME
     assert len(rt.weights) == 160, len(rt.weights)
+    assert len(rt.geglu_modules) == 16, len(rt.geglu_modules)   # every feed-forward GEGLU gated in the GEMM
     assert rt.attn.counts["gpu"] > 0 and rt.attn.decision, "attention never reached the fused kernel"
     assert all(e <= 0.1 for e in rt.attn.max_err.values())
     assert torch.isfinite(y2).all()
     assert rel_l2_err(y2, ref) < 3e-2, rel_l2_err(y2, ref)
     assert rel_l2_err(y1, y2) < 1e-6
     status = cn.NODE_CLASS_MAPPINGS["B200Status"]().status(None)["result"][0]
-    assert "NpuGemm[B200]" in status and "layers on GPU kernels: 160" in status
+    assert "NpuGemm[B200]" in status and "layers on GPU kernels: 160" in status and "GEGLU blocks fused: 16" in status
     cn.NODE_CLASS_MAPPINGS["B200Release"]().release(patched)
     assert not rt.installed
     assert all(not isinstance(m.forward, types.MethodType) or m.forward.__func__ is not cn._gpu_linear_forward
                for m in model.modules() if isinstance(m, torch.nn.Linear))
+    assert all(not isinstance(m.forward, types.MethodType) or m.forward.__func__ is not cn._gpu_geglu_forward
+               for m in model.modules())
 
 
 def test_unet_against_cpu_oracle(cuda_device, unet_pair):
