@@ -432,17 +432,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             } else {
               tmem_wait_ld();
               if (splits > 1) {
-                // Fixed summation order over the splits, this split's own partial taken from TMEM.
+                // Fixed summation order over the splits, this split's own partial taken from TMEM. The partials
+                // sit in L2 and each pass costs a round trip there, so two splits' loads go out per pass.
+                const float* part0 = args.ws_partial + size_t(tile) * splits * BN * kGemmBM + c * kGemmBM + row;
+                const size_t slab = size_t(BN) * kGemmBM;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = 0.0f;
-                for (int sp = 0; sp < splits; ++sp) {
+#pragma unroll 1
+                for (int sp = 0; sp < splits; sp += 2) {
+                  float p0[32], p1[32];
+                  const bool two = sp + 1 < splits;
                   if (sp == split) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r[j]);
+                    for (int j = 0; j < 32; ++j) p0[j] = __uint_as_float(r[j]);
                   } else {
-                    const float* part = args.ws_partial + (size_t(tile) * splits + sp) * BN * kGemmBM;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] += __ldcg(part + (c + j) * kGemmBM + row);
+                    for (int j = 0; j < 32; ++j) p0[j] = __ldcg(part0 + sp * slab + j * kGemmBM);
+                  }
+                  if (two && sp + 1 == split) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) p1[j] = __uint_as_float(r[j]);
+                  } else if (two) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) p1[j] = __ldcg(part0 + (sp + 1) * slab + j * kGemmBM);
+                  }
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] += p0[j];
+                  if (two) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] += p1[j];
                   }
                 }
 #pragma unroll
@@ -577,8 +595,9 @@ constexpr size_t kSplitCounterBytes = 4096;
 
 // Modelled time (SM clocks) of a plan: waves of persistent work units x per-unit time. A unit's main loop is
 // bounded by the larger of the tensor-core time (2*BN clocks per 64-deep K block at 8192 FLOP/clk/SM) and the
-// time to stream its operands into shared memory (~64 B/clk/SM); each unit pays a fixed pipeline fill, and a
-// split tile pays for writing and re-reading its f32 partials.
+// time to stream its operands into shared memory (~64 B/clk/SM); each unit pays a fixed pipeline fill. A split
+// tile pays for publishing its f32 partial and for the last split's reduction, which is latency-bound: per
+// 32-column chunk one L2 round trip (~1050 clocks measured) per two splits.
 double plan_cost(int64_t M, int64_t N, int64_t kb, int bn, int splits, int sms) {
   const int64_t tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + bn - 1) / bn);
   const int64_t units = tiles * splits;
@@ -587,7 +606,7 @@ double plan_cost(int64_t M, int64_t N, int64_t kb, int bn, int splits, int sms) 
   const double mma = 2.0 * bn;
   const double load = (kGemmBM + bn) * 128.0 / 64.0;
   double t = double(kb_unit) * std::max(mma, load) + 1500.0 + 8.0 * bn;
-  if (splits > 1) t += 8.0 * bn + 8.0 * bn * (splits - 1) + 1000.0;
+  if (splits > 1) t += 1000.0 + (bn / 32.0) * (300.0 + 1050.0 * double((splits + 1) / 2));
   return double(waves) * t;
 }
 }  // namespace
