@@ -77,3 +77,55 @@ def test_sharded_sampling_matches_single_process(tmp_path, P):
     # equal up to float reassociation: CPU matmuls block differently for different batch sizes (~1e-6 relative)
     scale = float(single.abs().max())
     assert torch.allclose(sharded, single, rtol=1e-4, atol=1e-5 * scale), float((sharded - single).abs().max())
+
+
+def _failing_worker(rank, world, port, P, out_dir, mode):
+    """A rank of a sharded run in which rank 1 fails on the host: it raises before the latent gather ("raises")
+    or never joins the process group ("never_joins"). Every rank records how its run ended."""
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    path = os.path.join(out_dir, f"rank{rank}.txt")
+    if mode == "never_joins" and rank == 1:
+        with open(path, "w") as f:
+            f.write("left")
+        return
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    except Exception as e:  # noqa: BLE001 - the outcome is what the test checks
+        with open(path, "w") as f:
+            f.write(f"init failed: {type(e).__name__}")
+        return
+    try:
+        torch.set_num_threads(1)
+        model = _tiny_unet()
+        lat, ctx, unc = _inputs(P)
+        if mode == "raises" and rank == 1:
+            raise RuntimeError("injected host-side failure before the gather")
+        with torch.no_grad():
+            sample_sharded(model, lat, ctx, unc, steps=1)
+        outcome = "ok"
+    except Exception as e:  # noqa: BLE001
+        outcome = f"failed: {type(e).__name__}"
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+    with open(path, "w") as f:
+        f.write(outcome)
+
+
+@pytest.mark.parametrize("mode", ["raises", "never_joins"])
+def test_rank_failure_surfaces_as_error_on_the_other_rank(tmp_path, mode):
+    """Failure detection for the sharded path without any GPU: when one rank fails on the host, the surviving
+    rank's collective (or rendezvous) ends with an exception within the process group's timeout instead of
+    waiting for good."""
+    import time
+    t0 = time.time()
+    mp.start_processes(_failing_worker, args=(2, _free_port(), 2, str(tmp_path), mode), nprocs=2, join=True,
+                       start_method="spawn")
+    assert time.time() - t0 < 120
+    survivor = (tmp_path / "rank0.txt").read_text()
+    assert survivor.startswith(("failed", "init failed")), survivor
