@@ -20,6 +20,7 @@ from __future__ import annotations
 import threading
 import time
 import types
+import weakref
 
 import numpy as np
 import torch
@@ -123,6 +124,12 @@ class B200Runtime:
         self.weights: dict[int, tuple] = {}      # id(module) -> (NpuWeight, bias tensor | None, name)
         self.installed: dict[int, tuple] = {}    # id(module) -> (module, original forward)
         self.geglu_modules: set[int] = set()     # GEGLU modules routed to the fused projection + gating kernel
+        # Sibling projections fed the same input (self-attention q/k/v, cross-attention k/v) run as ONE GEMM over
+        # the concatenated weight: leader id -> (fused NpuWeight, fused bias | None, [(member id, column slice)]),
+        # member id -> leader id; `pending` holds the member outputs of the last leader call until consumed.
+        self.fused_groups: dict[int, tuple] = {}
+        self.fused_member: dict[int, int] = {}
+        self.pending: dict[int, tuple] = {}
         self.enabled = False
         self.record_only = False
         self.recorded: set[tuple[int, int, int]] = set()
@@ -146,6 +153,7 @@ class B200Runtime:
             self.installed[id(mod)] = (mod, mod.forward)
             mod.forward = types.MethodType(_gpu_linear_forward, mod)
             n_new += 1
+        self._fuse_projections(diffusion_model)
         # GEGLU feed-forward blocks whose projection was taken over: projection + gating in one kernel.
         for name, mod in diffusion_model.named_modules():
             proj = getattr(mod, "proj", None)
@@ -156,11 +164,46 @@ class B200Runtime:
                 mod.forward = types.MethodType(_gpu_geglu_forward, mod)
         return n_new
 
+    def _fuse_projections(self, diffusion_model: torch.nn.Module) -> None:
+        """q/k/v of an attention module with one input width become one GEMM (to_q leads); otherwise k/v with
+        one input width (cross-attention on the text context) become one GEMM (to_k leads)."""
+        for mod in diffusion_model.modules():
+            lins = [getattr(mod, n, None) for n in ("to_q", "to_k", "to_v")]
+            if not all(isinstance(m, torch.nn.Linear) and id(m) in self.weights for m in lins):
+                continue
+            if any(id(m) in self.fused_member or id(m) in self.fused_groups for m in lins):
+                continue
+            q, k, v = lins
+            if q.in_features == k.in_features == v.in_features:
+                group = [q, k, v]
+            elif k.in_features == v.in_features:
+                group = [k, v]
+            else:
+                continue
+            w = torch.cat([m.weight.detach() for m in group])
+            nw = self.gemm.upload_weight(w, layout="nk")
+            bias = None
+            if any(m.bias is not None for m in group):
+                bias = torch.cat([m.bias.detach().float() if m.bias is not None else
+                                  torch.zeros(m.out_features, device=m.weight.device) for m in group])
+                bias = bias.to(self.gemm.device, torch.float32).contiguous()
+            members, col = [], group[0].out_features
+            for m in group[1:]:
+                members.append((id(m), col, col + m.out_features))
+                self.fused_member[id(m)] = id(group[0])
+                col += m.out_features
+            self.fused_groups[id(group[0])] = (nw, bias, members, group[0].out_features)
+
     def release(self) -> None:
         for mod, orig in self.installed.values():
             mod.forward = orig
         for w, _, _ in self.weights.values():
             w.release()
+        for nw, _, _, _ in self.fused_groups.values():
+            nw.release()
+        self.fused_groups.clear()
+        self.fused_member.clear()
+        self.pending.clear()
         self.installed.clear()
         self.weights.clear()
         self.geglu_modules.clear()
@@ -179,6 +222,21 @@ def _gpu_linear_forward(self: torch.nn.Linear, x: torch.Tensor) -> torch.Tensor:
             rt.recorded.add((tokens, w.K, w.N))
         return torch.nn.functional.linear(x, self.weight, self.bias)
     out_dtype = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
+    key = (x.data_ptr(), tuple(x.shape), tuple(x.stride()), x._version, out_dtype)
+    if id(self) in rt.fused_member:
+        hit = rt.pending.pop(id(self), None)
+        if hit is not None and hit[0] == key and hit[2]() is x:
+            return hit[1]  # computed by the group's leading projection on this very input tensor
+    group = rt.fused_groups.get(id(self))
+    if group is not None:
+        nw, fbias, members, n_own = group
+        y = rt.gemm.linear(x, nw, fbias, out_dtype=out_dtype)
+        if y.dtype != x.dtype:
+            y = y.to(dtype=x.dtype)
+        ref = weakref.ref(x)  # a later tensor at the same address can never match a freed input
+        for mid, c0, c1 in members:
+            rt.pending[mid] = (key, y[..., c0:c1], ref)
+        return y[..., :n_own]
     y = rt.gemm.linear(x, w, bias, out_dtype=out_dtype)
     return y if y.dtype == x.dtype else y.to(dtype=x.dtype)
 
@@ -398,8 +456,9 @@ class B200Status:
         if rt is None:
             s = "B200 runtime not started"
         else:
-            s = (rt.gemm.summary() + " | layers on GPU kernels: %d (GEGLU blocks fused: %d) | %s | last: %s"
-                 % (len(rt.weights), len(rt.geglu_modules), rt.attn.summary(), rt.last_summary))
+            s = (rt.gemm.summary() + " | layers on GPU kernels: %d (GEGLU blocks fused: %d, q/k/v groups in one GEMM: "
+                 "%d) | %s | last: %s" % (len(rt.weights), len(rt.geglu_modules), len(rt.fused_groups),
+                                          rt.attn.summary(), rt.last_summary))
         _log(s)
         return {"ui": {"text": [s]}, "result": (s,)}
 

@@ -83,6 +83,15 @@ def test_ragged_shapes(cuda_device, shape, variant):
     _check(_run(q, k, v, H, variant=variant), attention_ref(q, k, v, H))
 
 
+@pytest.mark.parametrize("shape", [(1, 2, 16384, 16384, 40), (2, 8, 16384, 77, 40)], ids=["self128x128", "cross128x128"])
+def test_long_sequences_128x128_latent(cuda_device, shape):
+    """The 128x128-latent blocks of the batched UNet config (self-attention over 16384 tokens, cross-attention to
+    77), which the reference's fused path cannot hold (its buffer caps send them to the CPU)."""
+    B, H, Sq, Skv, D = shape
+    q, k, v = _qkv(B, H, Sq, Skv, D, seed=16)
+    _check(_run(q, k, v, H), attention_ref(q, k, v, H))
+
+
 def test_head_dim_above_192_runs_one_query_tile(cuda_device):
     """d = 256 takes the one-query-tile kernel; asking for two query tiles per CTA is refused, not faked."""
     B, H, Sq, Skv, D = 1, 2, 300, 200, 256

@@ -76,6 +76,7 @@ def test_offload_node_end_to_end(cuda_device, unet_pair):
     rt = cn._RUNTIME
     assert len(rt.weights) == 160, len(rt.weights)
     assert len(rt.geglu_modules) == 16, len(rt.geglu_modules)   # every feed-forward GEGLU gated in the GEMM
+    assert len(rt.fused_groups) == 32, len(rt.fused_groups)     # 16 self-attention q/k/v + 16 cross k/v
     assert rt.attn.counts["gpu"] > 0 and rt.attn.decision, "attention never reached the fused kernel"
     assert all(e <= 0.1 for e in rt.attn.max_err.values())
     assert torch.isfinite(y2).all()
@@ -134,3 +135,40 @@ def test_runner_api_like_reference_scripts(cuda_device):
     assert rel_max_err(o, attention_ref(q, k, v, 4)) < 0.1
     s = g.summary()
     assert "calls" in s and g.stats["calls"] >= 3 and g.stats["attn_fused_calls"] >= 1
+
+
+def test_fused_projections_only_serve_the_same_input(cuda_device):
+    """q/k/v siblings run as one GEMM when fed the same tensor; a sibling fed another tensor (or called without
+    its leader) computes its own product, never a stale slice."""
+    from npu_ai_b200 import comfy_nodes as cn
+    from oracle import linear_ref
+
+    class Attn(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.to_q = torch.nn.Linear(320, 320, bias=False)
+            self.to_k = torch.nn.Linear(320, 320, bias=False)
+            self.to_v = torch.nn.Linear(320, 320, bias=False)
+
+    torch.manual_seed(0)
+    wrap = torch.nn.Module()
+    wrap.attn = Attn().to(cuda_device, torch.bfloat16)
+    rt = cn._get_runtime(cuda_device)
+    rt.take_over(wrap, 320, ())
+    rt.enabled = True
+    try:
+        assert id(wrap.attn.to_q) in rt.fused_groups
+        x = torch.randn(2, 300, 320, device=cuda_device).to(torch.bfloat16)
+        y = torch.randn(2, 300, 320, device=cuda_device).to(torch.bfloat16)
+        with torch.no_grad():
+            q = wrap.attn.to_q(x)
+            k_other = wrap.attn.to_k(y)       # different tensor: its own GEMM
+            v = wrap.attn.to_v(x)             # same tensor as the leader: the fused slice
+            k_alone = wrap.attn.to_k(x)       # the slice was consumed by now: computed again
+        for out, inp, m in ((q, x, wrap.attn.to_q), (k_other, y, wrap.attn.to_k), (v, x, wrap.attn.to_v),
+                            (k_alone, x, wrap.attn.to_k)):
+            ref = linear_ref(inp.cpu(), m.weight.cpu())
+            assert float((out.float().cpu() - ref).abs().max()) < 2e-2
+        assert v.stride(-2) == 960 and q.stride(-2) == 960      # slices of the one fused output
+    finally:
+        rt.release()
