@@ -165,8 +165,11 @@ class B200Runtime:
         return n_new
 
     def _fuse_projections(self, diffusion_model: torch.nn.Module) -> None:
-        """q/k/v of an attention module with one input width become one GEMM (to_q leads); otherwise k/v with
-        one input width (cross-attention on the text context) become one GEMM (to_k leads)."""
+        """q/k/v of an attention module with one input width become one GEMM (to_q leads). k/v projections of
+        cross-attention modules read the text context, which every block of a UNet call shares: all of them with
+        one input width become ONE grouped GEMM over the concatenated weights (the first block's to_k leads), so a
+        UNet call projects the context once instead of once per block."""
+        cross: dict[int, list] = {}
         for mod in diffusion_model.modules():
             lins = [getattr(mod, n, None) for n in ("to_q", "to_k", "to_v")]
             if not all(isinstance(m, torch.nn.Linear) and id(m) in self.weights for m in lins):
@@ -175,24 +178,26 @@ class B200Runtime:
                 continue
             q, k, v = lins
             if q.in_features == k.in_features == v.in_features:
-                group = [q, k, v]
+                self._add_group([q, k, v])
             elif k.in_features == v.in_features:
-                group = [k, v]
-            else:
-                continue
-            w = torch.cat([m.weight.detach() for m in group])
-            nw = self.gemm.upload_weight(w, layout="nk")
-            bias = None
-            if any(m.bias is not None for m in group):
-                bias = torch.cat([m.bias.detach().float() if m.bias is not None else
-                                  torch.zeros(m.out_features, device=m.weight.device) for m in group])
-                bias = bias.to(self.gemm.device, torch.float32).contiguous()
-            members, col = [], group[0].out_features
-            for m in group[1:]:
-                members.append((id(m), col, col + m.out_features))
-                self.fused_member[id(m)] = id(group[0])
-                col += m.out_features
-            self.fused_groups[id(group[0])] = (nw, bias, members, group[0].out_features)
+                cross.setdefault(k.in_features, []).extend([k, v])
+        for group in cross.values():
+            self._add_group(group)
+
+    def _add_group(self, group: list) -> None:
+        w = torch.cat([m.weight.detach() for m in group])
+        nw = self.gemm.upload_weight(w, layout="nk")
+        bias = None
+        if any(m.bias is not None for m in group):
+            bias = torch.cat([m.bias.detach().float() if m.bias is not None else
+                              torch.zeros(m.out_features, device=m.weight.device) for m in group])
+            bias = bias.to(self.gemm.device, torch.float32).contiguous()
+        members, col = [], group[0].out_features
+        for m in group[1:]:
+            members.append((id(m), col, col + m.out_features))
+            self.fused_member[id(m)] = id(group[0])
+            col += m.out_features
+        self.fused_groups[id(group[0])] = (nw, bias, members, group[0].out_features)
 
     def release(self) -> None:
         for mod, orig in self.installed.values():
