@@ -90,6 +90,29 @@ int npub200_gemm_geglu(const void* x, int64_t ldx, int64_t m, int64_t k, const v
                        size_t workspace_bytes, int variant, void* stream);
 
 /* ----------------------------------------------------------------------------------------------------------
+ * 3x3 convolution, stride 1, zero padding 1, as an implicit GEMM on the tensor cores: out[n, y, x, co] =
+ * bias[co] + sum over (dy, dx, ci) of in[n, y+dy-1, x+dx-1, ci] * weight[co, dy, dx, ci] (+ residual). The
+ * reference names im2col + GEMM convolutions (K = 2880-11520) as its next experiment (docs/03-next-steps.md:112-114)
+ * and runs its convolutions on the CPU; here the im2col is a shifted TMA box per tap, never materialised.
+ * x: NHWC bf16 [n][h][w][cin], dense; weight: [cout][3][3][cin] bf16, dense (a PyTorch [cout][cin][3][3] weight
+ * permuted once); out: [n*h*w][cout] rows (NHWC) with row stride ldo, bf16 or f32. bias: [cout], or with
+ * bias_img_stride > 0 one row per image (e.g. conv bias + a ResBlock's time embedding), f32 or bf16, or NULL.
+ * residual: bf16 [n*h*w][cout] rows with stride ldr, added after the bias, or NULL. Needs cin % 64 == 0, a width
+ * dividing 128, and a height that is a multiple of the rows a 128-pixel tile takes (128 / width, capped at the
+ * height); other shapes are NPUB200_EUNSUPPORTED. `variant`: 0 or an output-channel tile in
+ * {64, 96, 128, 160, 192, 256}. Allocates nothing.
+ * ---------------------------------------------------------------------------------------------------------- */
+int npub200_conv3x3(const void* x, int64_t n, int64_t h, int64_t w, int64_t cin, const void* weight, int64_t cout,
+                    const void* bias, int bias_dtype, int64_t bias_img_stride, const void* residual, int64_t ldr,
+                    void* out, int64_t ldo, int out_dtype, void* workspace, size_t workspace_bytes, int variant,
+                    void* stream);
+/* Workspace bytes npub200_conv3x3 uses to split K across CTAs when the output tiles are too few to fill the GPU
+ * (small images, many channels). The same rules as the GEMM's workspace: its first bytes are counters that must be
+ * zero when first used and are left zero; NULL or a smaller workspace runs without split-K. */
+int npub200_conv3x3_workspace_size(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant,
+                                   size_t* bytes_out);
+
+/* ----------------------------------------------------------------------------------------------------------
  * GEMM without a workspace, for callers that cannot allocate device memory (a host whose device memory is owned
  * by its own pool manager and may not grow during a request, an FFI binding holding only the pointers it was
  * given, code that must not call cudaMalloc because it synchronises the device). No counterpart in the reference:

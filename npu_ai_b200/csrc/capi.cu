@@ -323,6 +323,48 @@ int npub200_gemm_geglu(const void* x, int64_t ldx, int64_t m, int64_t k, const v
                              workspace_bytes, variant, stream, 1);
 }
 
+int npub200_conv3x3(const void* x, int64_t n, int64_t h, int64_t w, int64_t cin, const void* weight, int64_t cout,
+                    const void* bias, int bias_dtype, int64_t bias_img_stride, const void* residual, int64_t ldr,
+                    void* out, int64_t ldo, int out_dtype, void* workspace, size_t workspace_bytes, int variant,
+                    void* stream) {
+  if (out_dtype != NPUB200_DTYPE_BF16 && out_dtype != NPUB200_DTYPE_F32)
+    return fail(kErrInvalid, "unknown output dtype code %d", out_dtype);
+  if (bias_dtype != NPUB200_DTYPE_BF16 && bias_dtype != NPUB200_DTYPE_F32)
+    return fail(kErrInvalid, "unknown bias dtype code %d", bias_dtype);
+  if (bias_img_stride < 0) return fail(kErrInvalid, "negative bias row stride");
+  ConvProblem p;
+  memset(&p, 0, sizeof(p));
+  p.x = x;
+  p.n = n;
+  p.h = h;
+  p.w = w;
+  p.cin = cin;
+  p.wt = weight;
+  p.cout = cout;
+  p.bias = bias;
+  p.bias_f32 = bias_dtype == NPUB200_DTYPE_F32;
+  p.bias_img_stride = bias_img_stride;
+  p.residual = residual;
+  p.ldr = ldr;
+  p.out = out;
+  p.ldo = ldo;
+  p.out_f32 = out_dtype == NPUB200_DTYPE_F32;
+  p.variant = variant;
+  p.debug = g_debug_flags.load();
+  p.ws_split = workspace;
+  p.ws_split_bytes = workspace_bytes;
+  return conv3x3_launch(p, static_cast<cudaStream_t>(stream));
+}
+
+int npub200_conv3x3_workspace_size(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant,
+                                   size_t* bytes_out) {
+  if (bytes_out == nullptr) return fail(kErrInvalid, "null output pointer");
+  const DeviceInfo* d = nullptr;
+  if (int rc = current_device_info(&d)) return rc;
+  *bytes_out = conv3x3_workspace_bytes(n, h, w, cin, cout, variant, d->sms);
+  return kOk;
+}
+
 int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t weight, const void* bias,
                    int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace, size_t workspace_bytes,
                    int variant, void* stream) {

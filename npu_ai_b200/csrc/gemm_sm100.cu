@@ -15,7 +15,13 @@
 // GEGLU form (template flag): W holds 2N rows ([a; gate], the GEGLU projection of SD1.5's feed-forward block) and
 // out[:, j] = (x.W[j] + b[j]) * gelu(x.W[N+j] + b[N+j]), the exact (erf) GELU. A tile's BN accumulator columns are
 // BN/2 a-rows and the BN/2 matching gate rows (two TMA boxes per stage), so the epilogue gates in registers and
-// the 2N-column projection is never written to memory. The only layout requirement is TMA's: 16-byte aligned base and row strides (K % 8 == 0 for a
+// the 2N-column projection is never written to memory.
+// 3x3 convolution form (template mode): implicit GEMM over an NHWC input, M = images x H x W pixels, N = output
+// channels, K = 9 taps x input channels. The A tile of K block (tap, 64-channel block) is one 4-D TMA box of 64
+// channels x a 128-pixel patch of whole image rows, shifted by the tap; the out-of-range rows and columns of the
+// shift are TMA zeros, which is the convolution's zero padding. The weights are [Cout, 3, 3, Cin] (K-major) and the
+// output tile is 128 consecutive NHWC pixels, so the epilogue is the GEMM's. The epilogue can also add a per-image
+// bias row (conv bias + time embedding) and a residual tensor. The only layout requirement is TMA's: 16-byte aligned base and row strides (K % 8 == 0 for a
 // dense matrix); anything else is repacked by the host into a caller-provided workspace first.
 #include <algorithm>
 #include <cstdio>
@@ -36,6 +42,11 @@ struct GemmArgs {
   const void* bias;
   int bias_f32;
   int bias_n;     // bias entries (N, or 2N in the GEGLU form)
+  long long bias_img_stride;  // > 0: bias row per image (rows of bias_img_pixels output rows), else one bias row
+  int bias_img_pixels, bias_imgs;
+  const void* residual;       // bf16 [M, N] added in the epilogue (row stride ldr), or null
+  long long ldr;
+  int cv_w, cv_hw, cv_cblocks;  // 3x3 convolution form: image width, pixels per image, 64-channel blocks of Cin
   void* out;
   long long ldo;
   int out_f32;
@@ -69,14 +80,14 @@ struct GemmLayout {
 
 // Bias for 32 consecutive output columns starting at gcol (0 beyond N). Compile-time indices only, so the values
 // stay in registers; the loads are broadcasts (every thread of the warp reads the same addresses).
-__device__ __forceinline__ void load_bias32(const GemmArgs& a, int gcol, float (&b)[32]) {
+__device__ __forceinline__ void load_bias32(const GemmArgs& a, int gcol, float (&b)[32], long long row_off = 0) {
   if (a.bias == nullptr) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) b[j] = 0.0f;
     return;
   }
   if (a.bias_f32) {
-    const float* p = static_cast<const float*>(a.bias) + gcol;
+    const float* p = static_cast<const float*>(a.bias) + row_off + gcol;
     if (gcol + 32 <= a.bias_n && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -91,7 +102,7 @@ __device__ __forceinline__ void load_bias32(const GemmArgs& a, int gcol, float (
       for (int j = 0; j < 32; ++j) b[j] = (gcol + j < a.bias_n) ? __ldg(p + j) : 0.0f;
     }
   } else {
-    const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(a.bias) + gcol;
+    const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(a.bias) + row_off + gcol;
     if (gcol + 32 <= a.bias_n && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -146,6 +157,32 @@ __device__ __forceinline__ void store_row32_direct(const GemmArgs& a, int grow, 
   }
 }
 
+// v += residual[grow, gcol .. gcol+31] (bf16), predicated on the output bounds.
+__device__ __forceinline__ void add_residual32(const GemmArgs& a, int grow, int gcol, float (&v)[32]) {
+  if (grow >= a.M) return;
+  const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(a.residual) + (long long)grow * a.ldr + gcol;
+  if (gcol + 32 <= a.N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 t = *(reinterpret_cast<const uint4*>(p) + j);
+      const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[8 * j + 2 * e] += __uint_as_float(w[e] << 16);
+        v[8 * j + 2 * e + 1] += __uint_as_float(w[e] & 0xFFFF0000u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (gcol + j < a.N) v[j] += __bfloat162float(p[j]);
+  }
+}
+
+constexpr int kModePlain = 0;
+constexpr int kModeGeglu = 1;
+constexpr int kModeConv3x3 = 2;
+
 // GELU with the error function (torch's default `F.gelu`, approximate='none').
 __device__ __forceinline__ float gelu_erf(float y) { return 0.5f * y * (1.0f + erff(y * 0.70710678118654752f)); }
 
@@ -159,11 +196,27 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& m_
   }
 }
 
-template <int BN, int STAGES, bool GEGLU>
+template <int BN, int STAGES, int MODE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                              const __grid_constant__ CUtensorMap tm_out, const GemmArgs args) {
   using L = GemmLayout<BN, STAGES>;
+  constexpr bool GEGLU = MODE == kModeGeglu;
+  // A tile of K block kb for the output rows from m0: a 2-D box of x, or in the convolution form the input patch
+  // of tap kb / cblocks (kh, kw) and channel block kb % cblocks, shifted by (kh - 1, kw - 1).
+  auto load_x = [&](uint64_t* bar, uint8_t* dst, int kb, int m0) {
+    if constexpr (MODE == kModeConv3x3) {
+      const int tap = kb / args.cv_cblocks;
+      const int cb = kb - tap * args.cv_cblocks;
+      const int kh = tap / 3;
+      const int kw = tap - 3 * kh;
+      const int img = m0 / args.cv_hw;
+      const int h0 = (m0 - img * args.cv_hw) / args.cv_w;
+      tma_load_4d(&tm_x, bar, dst, cb * kGemmBK, kw - 1, h0 + kh - 1, img);
+    } else {
+      tma_load_2d(&tm_x, bar, dst, kb * kGemmBK, m0);
+    }
+  };
   // Output columns per tile: BN, or BN/2 gated columns in the GEGLU form (a then gate rows of W in the B tile).
   constexpr int kOutCols = GEGLU ? BN / 2 : BN;
   static_assert(!GEGLU || (BN % 64 == 0), "GEGLU tiles hold two halves of a multiple of 32 columns");
@@ -255,7 +308,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (pre > 0) {
             // stage already armed and its W tile in flight (first stages of the first unit)
-            tma_load_2d(&tm_x, &full[stage], sA + stage * L::kABytes, kb * kGemmBK, m0);
+            load_x(&full[stage], sA + stage * L::kABytes, kb, m0);
             --pre;
           } else {
             if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutProducer)) {
@@ -263,7 +316,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               break;
             }
             mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-            tma_load_2d(&tm_x, &full[stage], sA + stage * L::kABytes, kb * kGemmBK, m0);
+            load_x(&full[stage], sA + stage * L::kABytes, kb, m0);
             load_w(&full[stage], sB + stage * L::kBBytes, kb, nb);
           }
           ++issued;
@@ -418,7 +471,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint32_t r[32];
             tmem_ld32(t_row + uint32_t(c), r);
             float b[32];
-            load_bias32(args, n0 + c, b);
+            long long bias_row = 0;
+            if (args.bias_img_stride > 0)
+              bias_row = (long long)min((m0 + row) / args.bias_img_pixels, args.bias_imgs - 1) * args.bias_img_stride;
+            load_bias32(args, n0 + c, b, bias_row);
             float v[32];
             if constexpr (GEGLU) {
               uint32_t rg[32];
@@ -469,6 +525,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + b[j];
               }
+              if (args.residual != nullptr) add_residual32(args, m0 + row, n0 + c, v);
             }
             if (chunk_tma) {
               uint8_t* rowp = sb + lane * 128;
@@ -527,12 +584,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ---------------------------------------------------------------------------------------------------------------
 namespace {
 
-template <int BN, int STAGES, bool GEGLU = false>
+template <int BN, int STAGES, int MODE = kModePlain>
 int launch_variant(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mo, const GemmArgs& args,
                    int grid, cudaStream_t st, int device) {
   using L = GemmLayout<BN, STAGES>;
   static bool configured[64] = {false};
-  auto kern = gemm_bf16_tcgen05_kernel<BN, STAGES, GEGLU>;
+  auto kern = gemm_bf16_tcgen05_kernel<BN, STAGES, MODE>;
   if (device < 0 || device >= 64) return fail(kErrInvalid, "device ordinal %d out of range", device);
   if (!configured[device]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
@@ -686,6 +743,7 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   if (tma_store && encode_out_map(p.out, p.M, p.N, p.ldo, p.out_f32 != 0, &mo) != kOk) tma_store = false;
 
   GemmArgs a;
+  memset(&a, 0, sizeof(a));
   a.tma_store = tma_store ? 1 : 0;
   a.M = int(p.M);
   a.N = int(p.N);
@@ -717,10 +775,10 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
 
   if (geglu) {
     switch (bn) {
-      case 64: return launch_variant<64, 8, true>(mx, mw, mo, a, grid, stream, dev->device);
-      case 128: return launch_variant<128, 6, true>(mx, mw, mo, a, grid, stream, dev->device);
-      case 192: return launch_variant<192, 4, true>(mx, mw, mo, a, grid, stream, dev->device);
-      case 256: return launch_variant<256, 4, true>(mx, mw, mo, a, grid, stream, dev->device);
+      case 64: return launch_variant<64, 8, kModeGeglu>(mx, mw, mo, a, grid, stream, dev->device);
+      case 128: return launch_variant<128, 6, kModeGeglu>(mx, mw, mo, a, grid, stream, dev->device);
+      case 192: return launch_variant<192, 4, kModeGeglu>(mx, mw, mo, a, grid, stream, dev->device);
+      case 256: return launch_variant<256, 4, kModeGeglu>(mx, mw, mo, a, grid, stream, dev->device);
     }
     return fail(kErrUnsupported, "no GEGLU GEMM variant with an N tile of %d", bn);
   }
@@ -733,6 +791,115 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
     case 256: return launch_variant<256, 4>(mx, mw, mo, a, grid, stream, dev->device);
   }
   return fail(kErrUnsupported, "no GEMM variant with an N tile of %d", bn);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// 3x3 convolution (implicit GEMM, the kernel's convolution form)
+// ---------------------------------------------------------------------------------------------------------------
+int conv3x3_launch(const ConvProblem& p, cudaStream_t stream) {
+  const DeviceInfo* dev = nullptr;
+  if (int rc = current_device_info(&dev)) return rc;
+  if (p.x == nullptr || p.wt == nullptr || p.out == nullptr) return fail(kErrInvalid, "conv3x3: null pointer");
+  if (p.n <= 0 || p.h <= 0 || p.w <= 0 || p.cin <= 0 || p.cout <= 0)
+    return fail(kErrInvalid, "conv3x3 sizes must be positive");
+  if (p.cin % kGemmBK != 0)
+    return fail(kErrUnsupported, "conv3x3 needs input channels in multiples of 64 (got %lld)", (long long)p.cin);
+  // A tile is 128 output pixels made of whole image rows (and whole images when an image has fewer than 128).
+  if (p.w > 128 || 128 % p.w != 0)
+    return fail(kErrUnsupported, "conv3x3 needs an image width dividing 128 (got %lld)", (long long)p.w);
+  const int64_t th = std::min<int64_t>(p.h, 128 / p.w);
+  if (p.h % th != 0)
+    return fail(kErrUnsupported, "conv3x3: image height %lld is not a multiple of %lld rows", (long long)p.h,
+                (long long)th);
+  const int64_t imgs = 128 / (th * p.w);
+  if (th * p.w * imgs != 128)
+    return fail(kErrUnsupported, "conv3x3: %lld x %lld images do not tile 128 pixels", (long long)p.h, (long long)p.w);
+  const int64_t M = p.n * p.h * p.w, K = 9 * p.cin;
+  if (M > INT32_MAX / 2 || K > INT32_MAX / 2 || p.cout > INT32_MAX / 4) return fail(kErrInvalid, "conv3x3 too large");
+  if (reinterpret_cast<uintptr_t>(p.x) & 15 || reinterpret_cast<uintptr_t>(p.wt) & 15)
+    return fail(kErrInvalid, "conv3x3 input and weight must be 16-byte aligned");
+  if (p.ldo < p.cout) return fail(kErrInvalid, "conv3x3 output row stride below the channel count");
+  if (p.residual != nullptr && p.ldr < p.cout) return fail(kErrInvalid, "conv3x3 residual row stride too small");
+  if (p.variant) {
+    bool known = false;
+    for (int c : kTileChoices) known |= (c == p.variant);
+    if (!known) return fail(kErrUnsupported, "no conv3x3 variant with an output-channel tile of %d", p.variant);
+  }
+  GemmPlan plan = gemm_plan(M, p.cout, K, dev->sms, p.variant);
+  const int bn = plan.bn;
+  if (plan.splits > 1 && (p.ws_split == nullptr || p.ws_split_bytes < plan.split_ws_bytes ||
+                          (reinterpret_cast<uintptr_t>(p.ws_split) & 255) != 0)) {
+    plan.splits = 1;  // no room for partials: one CTA per tile over all of K
+    plan.kb_per_split = int(K / kGemmBK);
+  }
+
+  EncodeTiledFn enc = nullptr;
+  if (int rc = encode_tiled_fn(&enc)) return rc;
+  CUtensorMap mx, mw, mo;
+  {
+    cuuint64_t dims[4] = {cuuint64_t(p.cin), cuuint64_t(p.w), cuuint64_t(p.h), cuuint64_t(p.n)};
+    cuuint64_t strides[3] = {cuuint64_t(p.cin) * 2, cuuint64_t(p.w * p.cin) * 2, cuuint64_t(p.h * p.w * p.cin) * 2};
+    cuuint32_t box[4] = {cuuint32_t(kGemmBK), cuuint32_t(p.w), cuuint32_t(th), cuuint32_t(imgs)};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(p.x), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(kErrInvalid, "cuTensorMapEncodeTiled failed (%d) for the conv input", int(r));
+  }
+  if (int rc = encode_kmajor_map(p.wt, p.cout, K, K, bn, &mw)) return rc;
+  memset(&mo, 0, sizeof(mo));
+  const int esz = p.out_f32 ? 4 : 2;
+  bool tma_store = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && (p.ldo * esz) % 16 == 0;
+  if (tma_store && encode_out_map(p.out, M, p.cout, p.ldo, p.out_f32 != 0, &mo) != kOk) tma_store = false;
+
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.tma_store = tma_store ? 1 : 0;
+  a.M = int(M);
+  a.N = int(p.cout);
+  a.K = int(K);
+  a.num_m_blk = int((M + kGemmBM - 1) / kGemmBM);
+  a.num_n_blk = int((p.cout + bn - 1) / bn);
+  a.n_fastest = 1;  // the input patch stays in L2 while the output-channel tiles of a pixel tile go by
+  a.num_tiles = a.num_m_blk * a.num_n_blk;
+  a.num_kb = int(K / kGemmBK);
+  a.bias = p.bias;
+  a.bias_f32 = p.bias_f32;
+  a.bias_n = int(p.cout);
+  a.bias_img_stride = p.bias != nullptr ? p.bias_img_stride : 0;
+  a.bias_img_pixels = int(p.h * p.w);
+  a.bias_imgs = int(p.n);
+  a.residual = p.residual;
+  a.ldr = p.ldr;
+  a.out = p.out;
+  a.ldo = p.ldo;
+  a.out_f32 = p.out_f32;
+  a.splits = plan.splits;
+  a.kb_per_split = plan.kb_per_split;
+  a.ws_counter = plan.splits > 1 ? static_cast<unsigned int*>(p.ws_split) : nullptr;
+  a.ws_partial =
+      plan.splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(p.ws_split) + kSplitCounterBytes) : nullptr;
+  a.cv_w = int(p.w);
+  a.cv_hw = int(p.h * p.w);
+  a.cv_cblocks = int(p.cin / kGemmBK);
+  a.ctl.status = dev->status;
+  a.ctl.timeout_ns = wait_timeout_ns();
+  a.ctl.debug = p.debug;
+  const int grid = int(std::min<int64_t>(int64_t(a.num_tiles) * plan.splits, dev->sms));
+  switch (bn) {
+    case 64: return launch_variant<64, 8, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
+    case 96: return launch_variant<96, 6, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
+    case 128: return launch_variant<128, 6, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
+    case 160: return launch_variant<160, 5, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
+    case 192: return launch_variant<192, 4, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
+    case 256: return launch_variant<256, 4, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
+  }
+  return fail(kErrUnsupported, "no conv3x3 variant with an output-channel tile of %d", bn);
+}
+
+size_t conv3x3_workspace_bytes(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant, int sms) {
+  if (n <= 0 || h <= 0 || w <= 0 || cin <= 0 || cout <= 0 || sms <= 0) return 0;
+  return gemm_plan(n * h * w, cout, 9 * cin, sms, variant).split_ws_bytes;
 }
 
 // ---------------------------------------------------------------------------------------------------------------

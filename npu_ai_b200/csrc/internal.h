@@ -78,6 +78,29 @@ int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const 
                         int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream,
                         int geglu = 0);
 int gemm_launch(const GemmProblem& p, cudaStream_t stream);
+
+// 3x3 convolution, stride 1, zero padding 1, as an implicit GEMM on the GEMM kernel (its convolution form).
+struct ConvProblem {
+  const void* x;  // NHWC bf16 [n][h][w][cin], dense
+  int64_t n, h, w, cin;
+  const void* wt;  // [cout][3][3][cin] bf16, dense
+  int64_t cout;
+  const void* bias;           // [cout], or one row per image when bias_img_stride > 0; may be null
+  int bias_f32;
+  int64_t bias_img_stride;    // elements between the bias rows of consecutive images (0: one row for all)
+  const void* residual;       // bf16 [n*h*w, cout] added to the result (row stride ldr), or null
+  int64_t ldr;
+  void* out;                  // [n*h*w, cout] (NHWC), row stride ldo
+  int64_t ldo;
+  int out_f32;
+  int variant;                // 0 or a forced output-channel tile
+  uint32_t debug;
+  void* ws_split;             // split-K workspace (zeroed counters, then f32 partials), may be null
+  size_t ws_split_bytes;
+};
+int conv3x3_launch(const ConvProblem& p, cudaStream_t stream);
+// Split-K workspace bytes the convolution's fastest plan uses (0: none).
+size_t conv3x3_workspace_bytes(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant, int sms);
 // bf16 copy of a row-strided matrix into a dense [rows, cols_pad] buffer, zero-filling the pad columns.
 int repack_rows_bf16(const void* src, int64_t ld_src, int64_t rows, int64_t cols, void* dst, int64_t cols_pad,
                      cudaStream_t stream);

@@ -65,14 +65,20 @@ def _gemm_workspace(x: torch.Tensor, w: torch.Tensor | None, M: int, K: int, N: 
     _lib.call("npub200_gemm_workspace_size", ctypes.c_void_p(x.data_ptr()), x.stride(0), M, K,
               ctypes.c_void_p(w.data_ptr()) if w is not None else None, w.stride(0) if w is not None else 0, N,
               int(variant), ctypes.byref(nbytes))
-    if nbytes.value == 0:
+    return _workspace(x.device, nbytes.value)
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    """The zeroed per-(device, stream) workspace shared by the GEMM and convolution calls on that stream (grown to
+    a power of two, at least 4 MiB); their split-K counters are left zero by the kernels."""
+    if nbytes == 0:
         return None
-    key = (x.device.index or 0, torch.cuda.current_stream(x.device).cuda_stream)
+    key = (device.index or 0, torch.cuda.current_stream(device).cuda_stream)
     ws = _WORKSPACES.get(key)
-    if ws is None or ws.numel() < nbytes.value:
-        size = max(nbytes.value, 1 << 22)
+    if ws is None or ws.numel() < nbytes:
+        size = max(nbytes, 1 << 22)
         size = 1 << (size - 1).bit_length()
-        ws = torch.zeros(size, dtype=torch.uint8, device=x.device)
+        ws = torch.zeros(size, dtype=torch.uint8, device=device)
         _WORKSPACES[key] = ws
     return ws
 
@@ -154,6 +160,61 @@ def gemm_geglu(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = Non
                   ctypes.c_void_p(bias.data_ptr()) if bias is not None else None,
                   _DT[bias.dtype] if bias is not None else _lib.DTYPE_BF16,
                   ctypes.c_void_p(out.data_ptr()), out.stride(0), _DT[out.dtype],
+                  ctypes.c_void_p(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
+                  int(variant), ctypes.c_void_p(_stream_ptr(x.device)))
+    return out
+
+
+def pack_conv3x3_weight(w: torch.Tensor) -> torch.Tensor:
+    """PyTorch conv weight [cout, cin, 3, 3] -> the kernel's [cout, 3, 3, cin] bf16 layout (once per weight)."""
+    if w.dim() != 4 or tuple(w.shape[2:]) != (3, 3):
+        raise ValueError("expected a [cout, cin, 3, 3] convolution weight")
+    return w.detach().permute(0, 2, 3, 1).to(torch.bfloat16).contiguous()
+
+
+def conv3x3(x: torch.Tensor, w_packed: torch.Tensor, bias: torch.Tensor | None = None,
+            residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+            out_dtype: torch.dtype = torch.bfloat16, variant: int = 0) -> torch.Tensor:
+    """3x3 convolution (stride 1, zero padding 1) as an implicit GEMM, NHWC in and out.
+
+    x: bf16 [n, h, w, cin] contiguous (an NCHW channels_last tensor's `.permute(0, 2, 3, 1)` is such a view);
+    w_packed: from pack_conv3x3_weight; bias: [cout] or [n, cout] (one row per image), f32 or bf16; residual: bf16
+    [n, h, w, cout] added after the bias. Returns [n, h, w, cout].
+    """
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or w_packed.dtype != torch.bfloat16:
+        raise ValueError("conv3x3 operands must be bf16")
+    if x.dim() != 4 or not x.is_contiguous():
+        raise ValueError("conv3x3 input must be a contiguous [n, h, w, cin] (NHWC) tensor")
+    n, h, wd, cin = x.shape
+    if w_packed.dim() != 4 or tuple(w_packed.shape[1:]) != (3, 3, cin) or not w_packed.is_contiguous():
+        raise ValueError(f"conv3x3 weight must be a contiguous [cout, 3, 3, {cin}] tensor (pack_conv3x3_weight)")
+    cout = w_packed.shape[0]
+    if out is None:
+        out = torch.empty((n, h, wd, cout), dtype=out_dtype, device=x.device)
+    if out.dtype not in _DT or tuple(out.shape) != (n, h, wd, cout) or out.stride(-1) != 1 or \
+            out.stride(2) != out.stride(-2) or out.stride(1) != wd * out.stride(2) or out.stride(0) != h * out.stride(1):
+        raise ValueError("out must be [n, h, w, cout] with uniformly strided pixel rows")
+    img_stride = 0
+    if bias is not None:
+        if bias.dtype not in _DT or not bias.is_contiguous() or tuple(bias.shape) not in ((cout,), (n, cout)):
+            raise ValueError("bias must be a contiguous [cout] or [n, cout] f32/bf16 tensor")
+        img_stride = cout if bias.dim() == 2 else 0
+    ldr = 0
+    if residual is not None:
+        if residual.dtype != torch.bfloat16 or tuple(residual.shape) != (n, h, wd, cout) or residual.stride(-1) != 1 \
+                or residual.stride(0) != h * residual.stride(1) or residual.stride(1) != wd * residual.stride(2):
+            raise ValueError("residual must be a bf16 [n, h, w, cout] tensor with uniformly strided pixel rows")
+        ldr = residual.stride(2)
+    with torch.cuda.device(x.device):
+        nbytes = ctypes.c_size_t(0)
+        _lib.call("npub200_conv3x3_workspace_size", n, h, wd, cin, cout, int(variant), ctypes.byref(nbytes))
+        ws = _workspace(x.device, nbytes.value)
+        _lib.call("npub200_conv3x3", ctypes.c_void_p(x.data_ptr()), n, h, wd, cin, ctypes.c_void_p(w_packed.data_ptr()),
+                  cout, ctypes.c_void_p(bias.data_ptr()) if bias is not None else None,
+                  _DT[bias.dtype] if bias is not None else _lib.DTYPE_BF16, img_stride,
+                  ctypes.c_void_p(residual.data_ptr()) if residual is not None else None, ldr,
+                  ctypes.c_void_p(out.data_ptr()), out.stride(2), _DT[out.dtype],
                   ctypes.c_void_p(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
                   int(variant), ctypes.c_void_p(_stream_ptr(x.device)))
     return out

@@ -35,6 +35,21 @@ def geglu_ref(x: torch.Tensor, w_2n_k: torch.Tensor, bias: torch.Tensor | None =
     return a * F.gelu(gate)
 
 
+def conv3x3_ref(x_nhwc: torch.Tensor, w_oihw: torch.Tensor, bias: torch.Tensor | None = None,
+                residual: torch.Tensor | None = None) -> torch.Tensor:
+    """f32 3x3 convolution (stride 1, zero padding 1) on bf16-rounded operands, NHWC in and out: the CPU
+    convolution a SD1.5 UNet runs around the reference's offloaded layers (docs/02-results.md:411-413), restated with
+    `F.conv2d`. bias: [cout] or [n, cout] (one row per image); residual: [n, h, w, cout], added after the bias."""
+    x = bf16_round(x_nhwc).permute(0, 3, 1, 2)
+    y = F.conv2d(x, bf16_round(w_oihw), padding=1).permute(0, 2, 3, 1)
+    if bias is not None:
+        b = bias.detach().to("cpu").float()
+        y = y + (b[:, None, None, :] if b.dim() == 2 else b)
+    if residual is not None:
+        y = y + bf16_round(residual)
+    return y
+
+
 def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
                   head_major: bool = False) -> torch.Tensor:
     """f32 softmax(bf16(q) bf16(k)^T * scale) bf16(v) for every (batch, head) pair.
