@@ -112,6 +112,14 @@ int npub200_conv3x3(const void* x, int64_t n, int64_t h, int64_t w, int64_t cin,
 int npub200_conv3x3_workspace_size(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant,
                                    size_t* bytes_out);
 
+/* GroupNorm over NHWC bf16 activations, optionally followed by SiLU (the normalisation in front of each
+ * convolution of an SD1.5 ResBlock, which the reference leaves on the host, docs/02-results.md:411-413):
+ * out[n][p][ch] = act((x - mean_g) * rstd_g * gamma[ch] + beta[ch]) with the mean and variance of group g over all
+ * pixels and its c/groups channels, in f32. x, out: [n][hw][c] bf16 (NHWC, may alias), c % 8 == 0, 16-byte
+ * aligned; gamma, beta: f32 [c]; stats: caller scratch of 2 * n * groups floats. Deterministic; allocates nothing. */
+int npub200_group_norm(const void* x, int64_t n, int64_t hw, int64_t c, int64_t groups, const float* gamma,
+                       const float* beta, float eps, int apply_silu, void* out, float* stats, void* stream);
+
 /* ----------------------------------------------------------------------------------------------------------
  * GEMM without a workspace, for callers that cannot allocate device memory (a host whose device memory is owned
  * by its own pool manager and may not grow during a request, an FFI binding holding only the pointers it was

@@ -38,6 +38,8 @@ _SIGNATURES = {
                                        _c_p]),
     "npub200_conv3x3_workspace_size": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int,
                                                       ctypes.POINTER(ctypes.c_size_t)]),
+    "npub200_group_norm": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, ctypes.c_float, ctypes.c_int,
+                                          _c_p, _c_p, _c_p]),
     "npub200_gemm_noalloc": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p, ctypes.c_int,
                                             _c_p, _c_i64, ctypes.c_int, ctypes.c_int, _c_p]),
     "npub200_gemm_w": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, ctypes.c_int, _c_p, _c_i64,

@@ -130,6 +130,12 @@ class B200Runtime:
         self.fused_groups: dict[int, tuple] = {}
         self.fused_member: dict[int, int] = {}
         self.pending: dict[int, tuple] = {}
+        # Convolution-side takeover (channels-last activations): id(conv) -> (kind "3x3" | "1x1", packed weight or
+        # NpuWeight, f32 bias | None); id(GroupNorm) -> (f32 gamma, f32 beta); id(ResBlock) -> its fused plan.
+        self.convs: dict[int, tuple] = {}
+        self.norms: dict[int, tuple] = {}
+        self.resblocks: dict[int, tuple] = {}
+        self.conv_calls = 0  # convolution-side calls that ran on the B200 kernels (ResBlocks count once)
         self.enabled = False
         self.record_only = False
         self.recorded: set[tuple[int, int, int]] = set()
@@ -138,7 +144,8 @@ class B200Runtime:
         self.last_summary = ""
         self.attn = AttentionGate()
 
-    def take_over(self, diffusion_model: torch.nn.Module, min_features: int, skip: tuple[str, ...]) -> int:
+    def take_over(self, diffusion_model: torch.nn.Module, min_features: int, skip: tuple[str, ...],
+                  convolutions: bool = True) -> int:
         n_new = 0
         for name, mod in diffusion_model.named_modules():
             if not isinstance(mod, torch.nn.Linear) or id(mod) in self.installed:
@@ -154,6 +161,8 @@ class B200Runtime:
             mod.forward = types.MethodType(_gpu_linear_forward, mod)
             n_new += 1
         self._fuse_projections(diffusion_model)
+        if convolutions:
+            self._take_over_convs(diffusion_model)
         # GEGLU feed-forward blocks whose projection was taken over: projection + gating in one kernel.
         for name, mod in diffusion_model.named_modules():
             proj = getattr(mod, "proj", None)
@@ -184,6 +193,44 @@ class B200Runtime:
         for group in cross.values():
             self._add_group(group)
 
+    def _take_over_convs(self, dm: torch.nn.Module) -> None:
+        """3x3 convolutions (stride 1, padding 1, input channels in multiples of 64) onto the implicit-GEMM kernel,
+        1x1 convolutions onto the GEMM over the channels-last view, GroupNorms onto the NHWC GroupNorm kernel, and
+        ResBlocks built from those onto a fused forward (conv bias + time embedding as a per-image bias row of the
+        first convolution, the skip path as the residual of the second). Every patched forward falls back to the
+        module's own forward for inputs it does not take (not channels-last bf16 on the GPU, other shapes)."""
+        from . import kernels
+        dev = self.gemm.device
+        for mod in dm.modules():
+            if id(mod) in self.installed:
+                continue
+            if isinstance(mod, torch.nn.Conv2d) and mod.groups == 1 and mod.dilation == (1, 1) \
+                    and mod.padding_mode == "zeros":
+                bias = mod.bias.detach().to(dev, torch.float32).contiguous() if mod.bias is not None else None
+                if mod.kernel_size == (3, 3) and mod.stride == (1, 1) and mod.padding == (1, 1) \
+                        and mod.in_channels % 64 == 0:
+                    entry = ("3x3", kernels.pack_conv3x3_weight(mod.weight.to(dev)), bias)
+                elif mod.kernel_size == (1, 1) and mod.stride == (1, 1) and mod.padding == (0, 0) \
+                        and mod.in_channels % 8 == 0:
+                    w = mod.weight.detach().reshape(mod.out_channels, mod.in_channels)
+                    entry = ("1x1", self.gemm.upload_weight(w, layout="nk"), bias)
+                else:
+                    continue
+                self.convs[id(mod)] = entry
+                self.installed[id(mod)] = (mod, mod.forward)
+                mod.forward = types.MethodType(_gpu_conv_forward, mod)
+            elif isinstance(mod, torch.nn.GroupNorm) and mod.affine and mod.num_channels % 8 == 0:
+                self.norms[id(mod)] = (mod.weight.detach().to(dev, torch.float32).contiguous(),
+                                       mod.bias.detach().to(dev, torch.float32).contiguous())
+                self.installed[id(mod)] = (mod, mod.forward)
+                mod.forward = types.MethodType(_gpu_group_norm_forward, mod)
+        for mod in dm.modules():
+            plan = _resblock_plan(mod, self)
+            if plan is not None and id(mod) not in self.installed:
+                self.resblocks[id(mod)] = plan
+                self.installed[id(mod)] = (mod, mod.forward)
+                mod.forward = types.MethodType(_gpu_resblock_forward, mod)
+
     def _add_group(self, group: list) -> None:
         w = torch.cat([m.weight.detach() for m in group])
         nw = self.gemm.upload_weight(w, layout="nk")
@@ -206,6 +253,12 @@ class B200Runtime:
             w.release()
         for nw, _, _, _ in self.fused_groups.values():
             nw.release()
+        for kind, wt, _ in self.convs.values():
+            if kind == "1x1":
+                wt.release()
+        self.convs.clear()
+        self.norms.clear()
+        self.resblocks.clear()
         self.fused_groups.clear()
         self.fused_member.clear()
         self.pending.clear()
@@ -264,6 +317,126 @@ def _gpu_geglu_forward(self, x: torch.Tensor) -> torch.Tensor:
     out_dtype = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
     y = rt.gemm.linear_geglu(x, w, bias, out_dtype=out_dtype)
     return y if y.dtype == x.dtype else y.to(dtype=x.dtype)
+
+
+def _cl_bf16(x) -> bool:
+    """A channels-last bf16 CUDA activation (its NHWC view is contiguous)."""
+    return (isinstance(x, torch.Tensor) and x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 4
+            and x.is_contiguous(memory_format=torch.channels_last))
+
+
+def _conv_tiles(h: int, w: int) -> bool:
+    """Image shapes the implicit-GEMM convolution tiles: 128-pixel tiles of whole rows (or whole images)."""
+    if w > 128 or 128 % w:
+        return False
+    th = min(h, 128 // w)
+    return h % th == 0 and 128 % (th * w) == 0
+
+
+def _runtime_on(rt) -> bool:
+    return rt is not None and rt.enabled and not rt.record_only
+
+
+def _gpu_conv_forward(self, x: torch.Tensor) -> torch.Tensor:
+    """Conv2d.forward on the B200 kernels for channels-last bf16 activations: 3x3 on the implicit-GEMM
+    convolution, 1x1 on the GEMM; the result is channels-last."""
+    rt = _RUNTIME
+    entry = rt.convs.get(id(self)) if rt is not None else None
+    n, c, h, w = x.shape if x.dim() == 4 else (0, 0, 0, 0)
+    if entry is None or not _runtime_on(rt) or not _cl_bf16(x) or (entry[0] == "3x3" and not _conv_tiles(h, w)):
+        return rt.installed[id(self)][1](x) if rt is not None and id(self) in rt.installed else \
+            torch.nn.Conv2d.forward(self, x)
+    from . import kernels
+    rt.conv_calls += 1
+    kind, wt, bias = entry
+    if kind == "3x3":
+        out = torch.empty((n, self.out_channels, h, w), dtype=torch.bfloat16, device=x.device,
+                          memory_format=torch.channels_last)
+        kernels.conv3x3(x.permute(0, 2, 3, 1), wt, bias, out=out.permute(0, 2, 3, 1))
+        return out
+    y = rt.gemm.linear(x.permute(0, 2, 3, 1), wt, bias, out_dtype=torch.bfloat16)  # [n, h, w, cout]
+    return y.permute(0, 3, 1, 2)
+
+
+def _gpu_group_norm_forward(self, x: torch.Tensor) -> torch.Tensor:
+    """GroupNorm.forward on the NHWC GroupNorm kernel for channels-last bf16 activations (torch's own kernel would
+    reorder them to NCHW and back)."""
+    rt = _RUNTIME
+    entry = rt.norms.get(id(self)) if rt is not None else None
+    if entry is None or not _runtime_on(rt) or not _cl_bf16(x):
+        return rt.installed[id(self)][1](x) if rt is not None and id(self) in rt.installed else \
+            torch.nn.GroupNorm.forward(self, x)
+    from . import kernels
+    out = torch.empty_like(x, memory_format=torch.channels_last)
+    kernels.group_norm(x.permute(0, 2, 3, 1), self.num_groups, entry[0], entry[1], eps=self.eps,
+                       out=out.permute(0, 2, 3, 1))
+    return out
+
+
+def _resblock_plan(mod, rt):
+    """The fused plan of an SD-style ResBlock (in_layers = GroupNorm, SiLU, 3x3 conv; emb_layers = SiLU, Linear;
+    out_layers = GroupNorm, SiLU, [Dropout], 3x3 conv; skip = identity or 1x1 conv) whose parts were taken over,
+    or None. Blocks with up/down-sampling or scale-shift conditioning keep their own forward."""
+    if type(mod).__name__ != "ResBlock":
+        return None
+    if getattr(mod, "updown", False) or getattr(mod, "use_scale_shift_norm", False) or \
+            getattr(mod, "skip_t_emb", False) or getattr(mod, "exchange_temb_dims", False):
+        return None
+    try:
+        il, ol, el, skip = mod.in_layers, mod.out_layers, mod.emb_layers, mod.skip_connection
+    except AttributeError:
+        return None
+    if not (len(il) == 3 and isinstance(il[0], torch.nn.GroupNorm) and isinstance(il[1], torch.nn.SiLU)
+            and isinstance(il[2], torch.nn.Conv2d) and isinstance(ol[0], torch.nn.GroupNorm)
+            and isinstance(ol[1], torch.nn.SiLU) and isinstance(ol[-1], torch.nn.Conv2d)
+            and all(isinstance(m, torch.nn.Dropout) for m in list(ol)[2:-1])):
+        return None
+    if not (len(el) == 2 and isinstance(el[0], torch.nn.SiLU) and isinstance(el[1], torch.nn.Linear)):
+        return None
+    conv1, conv2 = il[2], ol[-1]
+    if rt.convs.get(id(conv1), ("",))[0] != "3x3" or rt.convs.get(id(conv2), ("",))[0] != "3x3":
+        return None
+    if id(il[0]) not in rt.norms or id(ol[0]) not in rt.norms:
+        return None
+    if not isinstance(skip, torch.nn.Identity) and rt.convs.get(id(skip), ("",))[0] != "1x1":
+        return None
+    return (il[0], conv1, ol[0], conv2, skip)
+
+
+def _gpu_resblock_forward(self, x, emb, *args, **kwargs):
+    """ResBlock.forward in four launches plus the small time-embedding Linear: GroupNorm+SiLU, conv1 with the
+    bias row of each image = conv bias + emb_layers(emb), GroupNorm+SiLU, conv2 with the skip path (x or its 1x1
+    convolution) added in the epilogue."""
+    rt = _RUNTIME
+    plan = rt.resblocks.get(id(self)) if rt is not None else None
+    if plan is None or not _runtime_on(rt) or not _cl_bf16(x) or self.training or args or \
+            any(k != "transformer_options" for k in kwargs) or not _conv_tiles(x.shape[2], x.shape[3]):
+        return rt.installed[id(self)][1](x, emb, *args, **kwargs)
+    from . import kernels
+    rt.conv_calls += 1
+    gn1, conv1, gn2, conv2, skip = plan
+    n, c, h, w = x.shape
+    xh = x.permute(0, 2, 3, 1)
+    t1 = torch.empty_like(xh)
+    g1 = rt.norms[id(gn1)]
+    kernels.group_norm(xh, gn1.num_groups, g1[0], g1[1], eps=gn1.eps, silu=True, out=t1)
+    e = self.emb_layers(emb).float()
+    b1 = rt.convs[id(conv1)][2]
+    rows = (e + b1 if b1 is not None else e).contiguous()  # [n, cout]: conv bias + time embedding per image
+    cout = conv1.out_channels
+    h1 = torch.empty((n, h, w, cout), dtype=torch.bfloat16, device=x.device)
+    kernels.conv3x3(t1, rt.convs[id(conv1)][1], rows, out=h1)
+    g2 = rt.norms[id(gn2)]
+    kernels.group_norm(h1, gn2.num_groups, g2[0], g2[1], eps=gn2.eps, silu=True, out=h1)
+    if isinstance(skip, torch.nn.Identity):
+        res = xh
+    else:
+        _kind, ws, bs = rt.convs[id(skip)]
+        res = rt.gemm.linear(xh, ws, bs, out_dtype=torch.bfloat16)
+    out = torch.empty((n, conv2.out_channels, h, w), dtype=torch.bfloat16, device=x.device,
+                      memory_format=torch.channels_last)
+    kernels.conv3x3(h1, rt.convs[id(conv2)][1], rt.convs[id(conv2)][2], residual=res, out=out.permute(0, 2, 3, 1))
+    return out
 
 
 def _gpu_attention_override(func, q, k, v, heads, mask=None, attn_precision=None, skip_reshape=False,
@@ -365,6 +538,9 @@ class B200LinearOffload:
                 "attn_min_tokens": ("INT", {"default": 256, "min": 1, "max": 65536,
                                             "tooltip": "attention calls with fewer query tokens use the model's "
                                                        "own attention"}),
+                "convolutions": ("BOOLEAN", {"default": True,
+                                             "tooltip": "also run 3x3/1x1 convolutions, GroupNorms and ResBlocks "
+                                                        "of channels-last bf16 models on the B200 kernels"}),
             },
         }
 
@@ -373,7 +549,8 @@ class B200LinearOffload:
     CATEGORY = "GPU/B200"
     DESCRIPTION = "Runs the model's Linear layers and attention on hand-written B200 (sm_100a) kernels."
 
-    def apply(self, model, enabled, min_tokens, min_features, skip_names, attention="auto", attn_min_tokens=256):
+    def apply(self, model, enabled, min_tokens, min_features, skip_names, attention="auto", attn_min_tokens=256,
+              convolutions=True):
         if not enabled:
             return (model,)
         rt = _get_runtime()
@@ -401,7 +578,7 @@ class B200LinearOffload:
                 if not state["prepared"]:
                     # Weights are taken after the ModelPatcher applied its patches (LoRA etc.), i.e. now.
                     t0 = time.perf_counter()
-                    n = rt.take_over(dm, int(min_features), skip)
+                    n = rt.take_over(dm, int(min_features), skip, bool(convolutions))
                     _log(f"took over {n} new Linear layers ({len(rt.weights)} total) in {time.perf_counter() - t0:.1f}s")
                     # One pass with the model's own ops records every (tokens, K, N) so the kernels are warmed up
                     # for each shape before the first accelerated run.

@@ -356,6 +356,12 @@ int npub200_conv3x3(const void* x, int64_t n, int64_t h, int64_t w, int64_t cin,
   return conv3x3_launch(p, static_cast<cudaStream_t>(stream));
 }
 
+int npub200_group_norm(const void* x, int64_t n, int64_t hw, int64_t c, int64_t groups, const float* gamma,
+                       const float* beta, float eps, int apply_silu, void* out, float* stats, void* stream) {
+  return group_norm_launch(x, n, hw, c, groups, gamma, beta, eps, apply_silu, out, stats,
+                           static_cast<cudaStream_t>(stream));
+}
+
 int npub200_conv3x3_workspace_size(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant,
                                    size_t* bytes_out) {
   if (bytes_out == nullptr) return fail(kErrInvalid, "null output pointer");

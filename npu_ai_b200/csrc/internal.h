@@ -99,6 +99,9 @@ struct ConvProblem {
   size_t ws_split_bytes;
 };
 int conv3x3_launch(const ConvProblem& p, cudaStream_t stream);
+// GroupNorm (+ SiLU) over NHWC bf16: x, out [n][hw][c]; gamma, beta f32 [c]; stats: n*groups float2 of scratch.
+int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t groups, const float* gamma,
+                      const float* beta, float eps, int apply_silu, void* out, float* stats, cudaStream_t stream);
 // Split-K workspace bytes the convolution's fastest plan uses (0: none).
 size_t conv3x3_workspace_bytes(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant, int sms);
 // bf16 copy of a row-strided matrix into a dense [rows, cols_pad] buffer, zero-filling the pad columns.

@@ -220,6 +220,38 @@ def conv3x3(x: torch.Tensor, w_packed: torch.Tensor, bias: torch.Tensor | None =
     return out
 
 
+_GN_STATS: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def group_norm(x: torch.Tensor, groups: int, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
+               silu: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """GroupNorm (optionally + SiLU) over a contiguous NHWC bf16 tensor [n, h, w, c] (a channels_last activation's
+    `.permute(0, 2, 3, 1)`); gamma, beta: [c]. Returns [n, h, w, c] bf16 (`out` may be `x`)."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or x.dim() != 4 or not x.is_contiguous():
+        raise ValueError("group_norm takes a contiguous bf16 [n, h, w, c] tensor")
+    n, h, w, c = x.shape
+    if c % groups:
+        raise ValueError(f"{c} channels do not split into {groups} groups")
+    g32 = gamma.detach().to(x.device, torch.float32).contiguous()
+    b32 = beta.detach().to(x.device, torch.float32).contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    if out.shape != x.shape or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 tensor shaped like x")
+    key = (x.device.index or 0, torch.cuda.current_stream(x.device).cuda_stream)
+    st = _GN_STATS.get(key)
+    if st is None or st.numel() < 2 * n * groups:
+        st = torch.empty(max(2 * n * groups, 4096), dtype=torch.float32, device=x.device)
+        _GN_STATS[key] = st
+    with torch.cuda.device(x.device):
+        _lib.call("npub200_group_norm", ctypes.c_void_p(x.data_ptr()), n, h * w, c, int(groups),
+                  ctypes.c_void_p(g32.data_ptr()), ctypes.c_void_p(b32.data_ptr()), ctypes.c_float(eps), int(silu),
+                  ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(st.data_ptr()),
+                  ctypes.c_void_p(_stream_ptr(x.device)))
+    return out
+
+
 def _bshd_strides(t: torch.Tensor, head_major: bool) -> tuple[int, int, int]:
     """(batch, seq, head) element strides of a (B, S, H, D) view given as (B, S, H*D) or (B, H, S, D)."""
     if head_major:

@@ -50,6 +50,17 @@ def conv3x3_ref(x_nhwc: torch.Tensor, w_oihw: torch.Tensor, bias: torch.Tensor |
     return y
 
 
+def group_norm_ref(x_nhwc: torch.Tensor, groups: int, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
+                   silu: bool = False) -> torch.Tensor:
+    """f32 `F.group_norm` (+ SiLU) on a bf16-rounded NHWC tensor, NHWC out: the host-side normalisation of a UNet
+    ResBlock around the reference's offloaded layers (docs/02-results.md:411-413)."""
+    x = bf16_round(x_nhwc).permute(0, 3, 1, 2)
+    y = F.group_norm(x, groups, gamma.detach().to("cpu").float(), beta.detach().to("cpu").float(), eps)
+    if silu:
+        y = F.silu(y)
+    return y.permute(0, 2, 3, 1)
+
+
 def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
                   head_major: bool = False) -> torch.Tensor:
     """f32 softmax(bf16(q) bf16(k)^T * scale) bf16(v) for every (batch, head) pair.

@@ -173,3 +173,29 @@ def test_fused_projections_only_serve_the_same_input(cuda_device):
         assert v.stride(-2) == 960 and q.stride(-2) == 960      # slices of the one fused output
     finally:
         rt.release()
+
+
+def test_unet_channels_last_on_conv_kernels(cuda_device):
+    """A channels-last bf16 UNet through the node with convolutions on: every ResBlock runs fused on the
+    implicit-GEMM convolution and NHWC GroupNorm kernels, 1x1 convolutions on the GEMM, and the output matches the
+    unpatched model (torch ops on the same GPU) within the tolerance of the Linear/attention path."""
+    from npu_ai_b200 import comfy_nodes as cn
+    from npu_ai_b200.sd15_unet import build_unet
+    model = build_unet(seed=1, device=cuda_device, dtype=torch.bfloat16).to(memory_format=torch.channels_last)
+    x, t, ctx = _inputs(32, device=cuda_device)
+    x = x.to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    ctx = ctx.to(torch.bfloat16)
+    base = FakeModelPatcher(model)
+    with torch.no_grad():
+        ref = base.apply_model(x, t, ctx).float()
+    (patched,) = cn.B200LinearOffload().apply(base, True, 64, 320, "time_embed,label_emb,emb_layers", "gpu", 64, True)
+    try:
+        with torch.no_grad():
+            y = patched.apply_model(x, t, ctx).float()
+        rt = cn._RUNTIME
+        assert len(rt.resblocks) == 22, len(rt.resblocks)
+        assert rt.conv_calls > 22, rt.conv_calls
+        assert torch.isfinite(y).all()
+        assert rel_l2_err(y, ref) < 3e-2, rel_l2_err(y, ref)
+    finally:
+        cn.B200Release().release(patched)
