@@ -78,6 +78,13 @@ int npub200_gemm_plan(int64_t m, int64_t n, int64_t k, int variant, int* tile_n_
 int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t weight, const void* bias,
                    int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace, size_t workspace_bytes,
                    int variant, void* stream);
+/* GEMM with a residual added in the epilogue: out = x . W^T + bias + residual, residual bf16 [M, N] with row
+ * stride ldr (may be `out` itself). The residual connections of a transformer block (x + to_out(attn),
+ * x + ff(..)), which the reference's host code adds after its offloaded Linear (npu/xdna1_gemm.py:428-448 returns
+ * the projection alone), land in the same kernel. Otherwise as npub200_gemm. */
+int npub200_gemm_residual(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                          const void* bias, int bias_dtype, const void* residual, int64_t ldr, void* out, int64_t ldo,
+                          int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream);
 /* GEGLU feed-forward projection in one kernel: W is [2n, K] (nn.Linear layout of SD1.5's GEGLU `proj`: the n
  * value rows, then the n gate rows), bias [2n] or NULL, and out[M, n] = (x.W[j] + b[j]) * gelu(x.W[n+j] + b[n+j])
  * with the exact (erf) GELU, f32 accumulation and gating, out f32 or bf16. The reference computes the projection
@@ -116,9 +123,13 @@ int npub200_conv3x3_workspace_size(int64_t n, int64_t h, int64_t w, int64_t cin,
  * convolution of an SD1.5 ResBlock, which the reference leaves on the host, docs/02-results.md:411-413):
  * out[n][p][ch] = act((x - mean_g) * rstd_g * gamma[ch] + beta[ch]) with the mean and variance of group g over all
  * pixels and its c/groups channels, in f32. x, out: [n][hw][c] bf16 (NHWC, may alias), c % 8 == 0, 16-byte
- * aligned; gamma, beta: f32 [c]; stats: caller scratch of 2 * n * groups floats. Deterministic; allocates nothing. */
+ * aligned; gamma, beta: f32 [c]; stats: caller scratch of npub200_group_norm_scratch_size() bytes, ZERO before its
+ * first use (it ends in ticket counters the kernels leave zero; one scratch per stream). Deterministic: the
+ * statistics pass splits each (image, group) over pixel slices and combines them in slice order. Allocates
+ * nothing. */
 int npub200_group_norm(const void* x, int64_t n, int64_t hw, int64_t c, int64_t groups, const float* gamma,
                        const float* beta, float eps, int apply_silu, void* out, float* stats, void* stream);
+int npub200_group_norm_scratch_size(int64_t n, int64_t groups, size_t* bytes_out);
 
 /* ----------------------------------------------------------------------------------------------------------
  * GEMM without a workspace, for callers that cannot allocate device memory (a host whose device memory is owned

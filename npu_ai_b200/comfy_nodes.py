@@ -136,6 +136,10 @@ class B200Runtime:
         self.norms: dict[int, tuple] = {}
         self.resblocks: dict[int, tuple] = {}
         self.conv_calls = 0  # convolution-side calls that ran on the B200 kernels (ResBlocks count once)
+        # Transformer blocks whose residual adds go into the output Linears' GEMM epilogues: id(block) ->
+        # (attn1 out Linear, attn2 out Linear, feed-forward out Linear); pending_res: id(Linear) -> residual.
+        self.tblocks: dict[int, tuple] = {}
+        self.pending_res: dict[int, torch.Tensor] = {}
         self.enabled = False
         self.record_only = False
         self.recorded: set[tuple[int, int, int]] = set()
@@ -161,6 +165,12 @@ class B200Runtime:
             mod.forward = types.MethodType(_gpu_linear_forward, mod)
             n_new += 1
         self._fuse_projections(diffusion_model)
+        for mod in diffusion_model.modules():
+            plan = _tblock_plan(mod, self)
+            if plan is not None and id(mod) not in self.installed:
+                self.tblocks[id(mod)] = plan
+                self.installed[id(mod)] = (mod, mod.forward)
+                mod.forward = types.MethodType(_gpu_tblock_forward, mod)
         if convolutions:
             self._take_over_convs(diffusion_model)
         # GEGLU feed-forward blocks whose projection was taken over: projection + gating in one kernel.
@@ -259,6 +269,8 @@ class B200Runtime:
         self.convs.clear()
         self.norms.clear()
         self.resblocks.clear()
+        self.tblocks.clear()
+        self.pending_res.clear()
         self.fused_groups.clear()
         self.fused_member.clear()
         self.pending.clear()
@@ -280,6 +292,11 @@ def _gpu_linear_forward(self: torch.nn.Linear, x: torch.Tensor) -> torch.Tensor:
             rt.recorded.add((tokens, w.K, w.N))
         return torch.nn.functional.linear(x, self.weight, self.bias)
     out_dtype = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
+    res = rt.pending_res.get(id(self))
+    if res is not None and out_dtype == torch.bfloat16 and res.dtype == torch.bfloat16 and \
+            tuple(res.shape) == (*x.shape[:-1], w.N) and res.is_contiguous():
+        del rt.pending_res[id(self)]  # consumed: the residual add happens in this GEMM's epilogue
+        return rt.gemm.linear(x, w, bias, out_dtype=out_dtype, residual=res)
     key = (x.data_ptr(), tuple(x.shape), tuple(x.stride()), x._version, out_dtype)
     if id(self) in rt.fused_member:
         hit = rt.pending.pop(id(self), None)
@@ -317,6 +334,63 @@ def _gpu_geglu_forward(self, x: torch.Tensor) -> torch.Tensor:
     out_dtype = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
     y = rt.gemm.linear_geglu(x, w, bias, out_dtype=out_dtype)
     return y if y.dtype == x.dtype else y.to(dtype=x.dtype)
+
+
+def _out_linear(m):
+    """The Linear at the end of an attention's to_out (a Linear, or Linear + Dropout) or a feed-forward's net."""
+    if isinstance(m, torch.nn.Linear):
+        return m
+    if isinstance(m, torch.nn.Sequential) and len(m) and isinstance(m[0], torch.nn.Linear) and \
+            all(isinstance(t, (torch.nn.Dropout, torch.nn.Identity)) for t in list(m)[1:]):
+        return m[0]
+    return None
+
+
+def _tblock_plan(mod, rt):
+    """(attn1 out Linear, attn2 out Linear, feed-forward out Linear) of an SD-style BasicTransformerBlock whose
+    three were taken over, or None."""
+    if type(mod).__name__ != "BasicTransformerBlock":
+        return None
+    try:
+        a1, a2, ff = mod.attn1, mod.attn2, mod.ff
+        mod.norm1, mod.norm2, mod.norm3
+        net = ff.net
+    except AttributeError:
+        return None
+    o1, o2 = _out_linear(getattr(a1, "to_out", None)), _out_linear(getattr(a2, "to_out", None))
+    o3 = net[-1] if isinstance(net, torch.nn.Sequential) and isinstance(net[-1], torch.nn.Linear) else None
+    if any(o is None or id(o) not in rt.weights for o in (o1, o2, o3)):
+        return None
+    return (o1, o2, o3)
+
+
+def _with_residual(rt, lin, res, fn):
+    """fn() with `res` offered to Linear `lin` as its epilogue residual; added here if the Linear did not take it
+    (its own forward ran, or shapes differed), so the result is x + f(x) either way."""
+    rt.pending_res[id(lin)] = res
+    try:
+        y = fn()
+    finally:
+        left = rt.pending_res.pop(id(lin), None)
+    return y + res if left is not None else y
+
+
+def _gpu_tblock_forward(self, x, context=None, transformer_options=None, **kwargs):
+    """BasicTransformerBlock.forward with its three residual adds in the output GEMMs' epilogues:
+    x = x + attn1(norm1 x); x = x + attn2(norm2 x, context); x = x + ff(norm3 x). Blocks with ComfyUI patches,
+    disabled self-attention or extra arguments keep their own forward."""
+    rt = _RUNTIME
+    to = transformer_options if transformer_options is not None else {}
+    plan = rt.tblocks.get(id(self)) if rt is not None else None
+    if (plan is None or not _runtime_on(rt) or kwargs or self.training or not x.is_cuda or x.dtype != torch.bfloat16
+            or not x.is_contiguous() or to.get("patches") or to.get("patches_replace")
+            or getattr(self, "disable_self_attn", False)):
+        return rt.installed[id(self)][1](x, context, transformer_options, **kwargs)
+    o1, o2, o3 = plan
+    x = _with_residual(rt, o1, x, lambda: self.attn1(self.norm1(x), context=None, transformer_options=to))
+    x = _with_residual(rt, o2, x, lambda: self.attn2(self.norm2(x), context=context, transformer_options=to))
+    x = _with_residual(rt, o3, x, lambda: self.ff(self.norm3(x)))
+    return x
 
 
 def _cl_bf16(x) -> bool:

@@ -171,7 +171,7 @@ size_t gemm_workspace_bytes(const void* x, int64_t ldx, int64_t m, int64_t k, co
 int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
                         const CUtensorMap* w_map, const void* bias, int bias_dtype, void* out, int64_t ldo,
                         int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream,
-                        int geglu) {
+                        int geglu, const void* residual, int64_t ldr) {
   if (int rc = check_gemm_common(m, k, n, bias_dtype, out, ldo, out_dtype)) return rc;
   if (x == nullptr || w == nullptr) return fail(kErrInvalid, "GEMM operand pointer is null");
   if (ldx < k) return fail(kErrInvalid, "x row stride %lld < K=%lld", (long long)ldx, (long long)k);
@@ -195,6 +195,10 @@ int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const 
   p.w_map_cache = w_map;
   p.debug = g_debug_flags.load();
   p.geglu = geglu;
+  if (residual != nullptr && ldr < n) return fail(kErrInvalid, "residual row stride %lld < N=%lld", (long long)ldr,
+                                                  (long long)n);
+  p.residual = residual;
+  p.ldr = ldr;
 
   const DeviceInfo* dev = nullptr;
   if (int rc = current_device_info(&dev)) return rc;
@@ -314,6 +318,15 @@ int npub200_gemm(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w
                      workspace_bytes, variant, stream);
 }
 
+int npub200_gemm_residual(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
+                          const void* bias, int bias_dtype, const void* residual, int64_t ldr, void* out, int64_t ldo,
+                          int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream) {
+  if (int rc = check_gemm_common(m, k, n, bias_dtype, out, ldo, out_dtype)) return rc;
+  if (residual == nullptr) return fail(kErrInvalid, "npub200_gemm_residual needs a residual");
+  return gemm_with_workspace(x, ldx, m, k, w, ldw, n, nullptr, bias, bias_dtype, out, ldo, out_dtype, workspace,
+                             workspace_bytes, variant, stream, 0, residual, ldr);
+}
+
 int npub200_gemm_geglu(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
                        const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace,
                        size_t workspace_bytes, int variant, void* stream) {
@@ -360,6 +373,13 @@ int npub200_group_norm(const void* x, int64_t n, int64_t hw, int64_t c, int64_t 
                        const float* beta, float eps, int apply_silu, void* out, float* stats, void* stream) {
   return group_norm_launch(x, n, hw, c, groups, gamma, beta, eps, apply_silu, out, stats,
                            static_cast<cudaStream_t>(stream));
+}
+
+int npub200_group_norm_scratch_size(int64_t n, int64_t groups, size_t* bytes_out) {
+  if (bytes_out == nullptr) return fail(kErrInvalid, "null output pointer");
+  if (n <= 0 || groups <= 0) return fail(kErrInvalid, "group_norm sizes must be positive");
+  *bytes_out = group_norm_scratch_bytes(n, groups);
+  return kOk;
 }
 
 int npub200_conv3x3_workspace_size(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant,

@@ -760,6 +760,8 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.bias = p.bias;
   a.bias_f32 = p.bias_f32;
   a.bias_n = int(geglu ? 2 * p.N : p.N);
+  a.residual = geglu ? nullptr : p.residual;
+  a.ldr = p.ldr;
   a.out = p.out;
   a.ldo = p.ldo;
   a.out_f32 = p.out_f32;

@@ -3,9 +3,10 @@
 // GroupNorm/LayerNorm, ..."); on B200 it matters because the convolutions run channels-last: torch's GroupNorm
 // converts such tensors to NCHW and back, which costs more than the normalisation itself.
 //
-// Two HBM-bound passes, deterministic (fixed-order reductions, no atomics):
-//   gn_stats_kernel  one block per (image, group): sum and sum of squares of the group's hw x cg values in f32,
-//                    written as (mean, rstd).
+// Two HBM-bound passes, deterministic (fixed-order reductions):
+//   gn_stats_kernel  blocks over (group, image, pixel slice): partial sums and sums of squares of the group's values
+//                    in f32; the last slice block of each (image, group) combines them in slice order into
+//                    (mean, rstd).
 //   gn_apply_kernel  8 channels (16 bytes) per thread: y = (x - mean) * rstd * gamma + beta, optionally SiLU,
 //                    bf16 out (same NHWC layout).
 #include <algorithm>
@@ -14,42 +15,53 @@
 #include "internal.h"
 
 namespace npub200 {
+
+constexpr int kGnMaxSlices = 32;       // pixel slices per (image, group) in the statistics pass
+constexpr int64_t kGnCounters = 65536;  // ticket counters at the start of the scratch: images x groups <= this
+
 namespace {
 
 constexpr int kStatsThreads = 256;
 
+// Statistics of group g of image img over pixel slice blockIdx.z: partial (sum, sum of squares) in f32. The last
+// slice block of the (image, group) to finish (ticket from `counters`, which it resets to zero) adds the partials in
+// slice order and writes (mean, rstd), so the result does not depend on which block finishes last.
 __global__ void __launch_bounds__(kStatsThreads)
-    gn_stats_kernel(const __nv_bfloat16* __restrict__ x, int hw, int c, int cg, float eps, float2* __restrict__ stats) {
+    gn_stats_kernel(const __nv_bfloat16* __restrict__ x, int hw, int c, int cg, float eps, float2* __restrict__ stats,
+                    float2* __restrict__ partials, unsigned int* __restrict__ counters) {
   const int img = blockIdx.y;
   const int g = blockIdx.x;
+  const int slices = gridDim.z;
+  const int slice = blockIdx.z;
+  const int p_begin = int((long long)hw * slice / slices);
+  const int p_end = int((long long)hw * (slice + 1) / slices);
   const __nv_bfloat16* base = x + (long long)img * hw * c + (long long)g * cg;
   float s = 0.f, ss = 0.f;
-  if ((cg & 1) == 0 && (c & 1) == 0) {
-    // pairs of channels (the group's first channel is even because cg and c are)
-    for (int p = threadIdx.x; p < hw; p += kStatsThreads) {
-      const __nv_bfloat162* row = reinterpret_cast<const __nv_bfloat162*>(base + (long long)p * c);
-      for (int k = 0; k < cg / 2; ++k) {
-        const float2 v = __bfloat1622float2(row[k]);
-        s += v.x + v.y;
-        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, ss));
-      }
+  if ((cg & 1) == 0) {
+    // channel pairs (c and cg even, so the group's first channel is even)
+    const int pairs = cg / 2;
+    for (int i = p_begin * pairs + threadIdx.x; i < p_end * pairs; i += kStatsThreads) {
+      const int p = i / pairs;
+      const int k = i - p * pairs;
+      const float2 v = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(base + (long long)p * c)[k]);
+      s += v.x + v.y;
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, ss));
     }
   } else {
-    for (int p = threadIdx.x; p < hw; p += kStatsThreads) {
-      const __nv_bfloat16* row = base + (long long)p * c;
-      for (int k = 0; k < cg; ++k) {
-        const float v = __bfloat162float(row[k]);
-        s += v;
-        ss = fmaf(v, v, ss);
-      }
+    for (int i = p_begin * cg + threadIdx.x; i < p_end * cg; i += kStatsThreads) {
+      const int p = i / cg;
+      const float v = __bfloat162float(base[(long long)p * c + (i - p * cg)]);
+      s += v;
+      ss = fmaf(v, v, ss);
     }
   }
-  // Fixed-order reduction: warp shuffles, then the 8 warp totals in order.
+  // Fixed-order reduction: warp shuffles, then the warp totals in order.
   for (int o = 16; o > 0; o >>= 1) {
     s += __shfl_xor_sync(0xffffffffu, s, o);
     ss += __shfl_xor_sync(0xffffffffu, ss, o);
   }
   __shared__ float ws[kStatsThreads / 32][2];
+  __shared__ int last;
   if ((threadIdx.x & 31) == 0) {
     ws[threadIdx.x >> 5][0] = s;
     ws[threadIdx.x >> 5][1] = ss;
@@ -61,10 +73,25 @@ __global__ void __launch_bounds__(kStatsThreads)
       ts += ws[w][0];
       tss += ws[w][1];
     }
-    const float cnt = float(hw) * float(cg);
-    const float mean = ts / cnt;
-    const float var = fmaxf(tss / cnt - mean * mean, 0.f);
-    stats[img * gridDim.x + g] = make_float2(mean, rsqrtf(var + eps));
+    const int slot = img * gridDim.x + g;
+    __stcg(&partials[(long long)slot * slices + slice], make_float2(ts, tss));
+    __threadfence();
+    const unsigned int ticket = atomicAdd(&counters[slot], 1u);
+    last = ticket == unsigned(slices - 1);
+    if (last) {
+      __threadfence();
+      float as = 0.f, ass = 0.f;
+      for (int i = 0; i < slices; ++i) {
+        const float2 pv = __ldcg(&partials[(long long)slot * slices + i]);
+        as += pv.x;
+        ass += pv.y;
+      }
+      const float cnt = float(hw) * float(cg);
+      const float mean = as / cnt;
+      const float var = fmaxf(ass / cnt - mean * mean, 0.f);
+      stats[slot] = make_float2(mean, rsqrtf(var + eps));
+      counters[slot] = 0u;  // left zero for the next call
+    }
   }
 }
 
@@ -103,6 +130,12 @@ __global__ void gn_apply_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, long l
 
 }  // namespace
 
+size_t group_norm_scratch_bytes(int64_t n, int64_t groups) {
+  // Fixed region of zero-initialised ticket counters first (the same place whatever the sizes, so a scratch reused
+  // across shapes always finds them zero), then (mean, rstd) per (image, group), then the slice partials.
+  return size_t(kGnCounters) * 4 + size_t(n * groups) * (8 + 8 * kGnMaxSlices);
+}
+
 int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t groups, const float* gamma,
                       const float* beta, float eps, int apply_silu, void* out, float* stats, cudaStream_t stream) {
   const DeviceInfo* dev = nullptr;
@@ -114,16 +147,26 @@ int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t g
                 (long long)hw, (long long)c, (long long)groups);
   if (c % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
     return fail(kErrUnsupported, "group_norm needs c %% 8 == 0 and 16-byte aligned tensors");
-  if (n > 65535 || groups > INT32_MAX || hw > INT32_MAX / 2) return fail(kErrInvalid, "group_norm: too large");
-  gn_stats_kernel<<<dim3(unsigned(groups), unsigned(n)), kStatsThreads, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(x), int(hw), int(c), int(c / groups), eps, reinterpret_cast<float2*>(stats));
+  if (n > 65535 || groups > 65535 || n * groups > kGnCounters || hw > INT32_MAX / 64 ||
+      hw * (c / groups) > INT32_MAX)
+    return fail(kErrInvalid, "group_norm: too large (images x groups <= %lld)", (long long)kGnCounters);
+  // Pixel slices per (image, group): enough blocks to fill the GPU, each with at least a few thousand values.
+  const int64_t cg = c / groups;
+  int64_t slices = std::max<int64_t>(1, (int64_t(dev->sms) * 4 + n * groups - 1) / (n * groups));
+  slices = std::min<int64_t>({slices, int64_t(kGnMaxSlices), std::max<int64_t>(1, hw * cg / 4096)});
+  unsigned int* counters = reinterpret_cast<unsigned int*>(stats);         // [kGnCounters]
+  float* st = stats + kGnCounters;                                         // [n * groups] float2
+  float* partials = st + 2 * n * groups;                                   // [n * groups * slices] float2
+  gn_stats_kernel<<<dim3(unsigned(groups), unsigned(n), unsigned(slices)), kStatsThreads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), int(hw), int(c), int(cg), eps, reinterpret_cast<float2*>(st),
+      reinterpret_cast<float2*>(partials), counters);
   if (int rc = check_cuda(cudaGetLastError(), "group_norm stats launch")) return rc;
   const long long total = n * hw * (c / 8);
   const int threads = 256;
   const int grid = int(std::min<long long>((total + threads - 1) / threads, (long long)dev->sms * 16));
   gn_apply_kernel<<<grid, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out),
                                                 n * hw, int(hw), int(c), int(c / groups), int(groups),
-                                                reinterpret_cast<const float2*>(stats), gamma, beta, apply_silu);
+                                                reinterpret_cast<const float2*>(st), gamma, beta, apply_silu);
   return check_cuda(cudaGetLastError(), "group_norm apply launch");
 }
 

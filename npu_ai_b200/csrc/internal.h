@@ -59,6 +59,8 @@ struct GemmProblem {
   size_t ws_split_bytes;
   uint32_t debug;
   int geglu;  // 1: W has 2N rows [a; gate] and out[:, j] = (x.W[j] + b[j]) * gelu(x.W[N+j] + b[N+j]); bias has 2N
+  const void* residual;  // bf16 [M, N] added after the bias (row stride ldr), or null
+  int64_t ldr;
 };
 // Launch plan for a problem: the N tile and the split-K factor (what `variant == 0` resolves to).
 struct GemmPlan {
@@ -76,7 +78,7 @@ size_t gemm_workspace_bytes(const void* x, int64_t ldx, int64_t m, int64_t k, co
 int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
                         const CUtensorMap* w_map, const void* bias, int bias_dtype, void* out, int64_t ldo,
                         int out_dtype, void* workspace, size_t workspace_bytes, int variant, void* stream,
-                        int geglu = 0);
+                        int geglu = 0, const void* residual = nullptr, int64_t ldr = 0);
 int gemm_launch(const GemmProblem& p, cudaStream_t stream);
 
 // 3x3 convolution, stride 1, zero padding 1, as an implicit GEMM on the GEMM kernel (its convolution form).
@@ -99,7 +101,9 @@ struct ConvProblem {
   size_t ws_split_bytes;
 };
 int conv3x3_launch(const ConvProblem& p, cudaStream_t stream);
-// GroupNorm (+ SiLU) over NHWC bf16: x, out [n][hw][c]; gamma, beta f32 [c]; stats: n*groups float2 of scratch.
+// GroupNorm (+ SiLU) over NHWC bf16: x, out [n][hw][c]; gamma, beta f32 [c]; stats: group_norm_scratch_bytes()
+// of scratch whose counters (the last n*groups words) are zero on first use and left zero.
+size_t group_norm_scratch_bytes(int64_t n, int64_t groups);
 int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t groups, const float* gamma,
                       const float* beta, float eps, int apply_silu, void* out, float* stats, cudaStream_t stream);
 // Split-K workspace bytes the convolution's fastest plan uses (0: none).

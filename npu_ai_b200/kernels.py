@@ -90,11 +90,13 @@ def reset_workspaces() -> None:
 
 
 def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
-         out_dtype: torch.dtype = torch.float32, variant: int = 0, handle: int | None = None) -> torch.Tensor:
-    """out[M, N] = x[M, K] @ w[N, K]^T (+ bias) with bf16 operands and f32 accumulation.
+         out_dtype: torch.dtype = torch.float32, variant: int = 0, handle: int | None = None,
+         residual: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] = x[M, K] @ w[N, K]^T (+ bias) (+ residual) with bf16 operands and f32 accumulation.
 
-    x and w are bf16 CUDA matrices with a unit inner stride (any row stride); bias is bf16 or f32 [N]. With
-    `handle` (from register_weight for this very `w`) the cached weight descriptor is used.
+    x and w are bf16 CUDA matrices with a unit inner stride (any row stride); bias is bf16 or f32 [N]; residual a
+    bf16 [M, N] matrix with unit inner stride (may be `out`). With `handle` (from register_weight for this very `w`)
+    the cached weight descriptor is used.
     """
     _require_cuda(x, "x")
     if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
@@ -112,6 +114,11 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out
     if bias is not None:
         if bias.dtype not in _DT or bias.numel() != N or not bias.is_contiguous():
             raise ValueError("bias must be a contiguous [N] bf16/f32 vector")
+    if residual is not None:
+        if residual.dtype != torch.bfloat16 or residual.dim() != 2 or tuple(residual.shape) != (M, N) or \
+                residual.stride(1) != 1:
+            raise ValueError("residual must be a bf16 [M, N] matrix with contiguous rows")
+        handle = None  # the residual entry point takes the weight itself
     ws = _gemm_workspace(x, None if handle is not None else w, M, K, N, variant)
     args_tail = (ctypes.c_void_p(bias.data_ptr()) if bias is not None else None,
                  _DT[bias.dtype] if bias is not None else _lib.DTYPE_BF16,
@@ -119,7 +126,11 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out
                  ctypes.c_void_p(ws.data_ptr()) if ws is not None else None, ws.numel() if ws is not None else 0,
                  int(variant), ctypes.c_void_p(_stream_ptr(x.device)))
     with torch.cuda.device(x.device):
-        if handle is not None:
+        if residual is not None:
+            _lib.call("npub200_gemm_residual", ctypes.c_void_p(x.data_ptr()), x.stride(0), M, K,
+                      ctypes.c_void_p(w.data_ptr()), w.stride(0), N, args_tail[0], args_tail[1],
+                      ctypes.c_void_p(residual.data_ptr()), residual.stride(0), *args_tail[2:])
+        elif handle is not None:
             _lib.call("npub200_gemm_w", ctypes.c_void_p(x.data_ptr()), x.stride(0), M, K, int(handle), *args_tail)
         else:
             _lib.call("npub200_gemm", ctypes.c_void_p(x.data_ptr()), x.stride(0), M, K, ctypes.c_void_p(w.data_ptr()),
@@ -239,10 +250,13 @@ def group_norm(x: torch.Tensor, groups: int, gamma: torch.Tensor, beta: torch.Te
         out = torch.empty_like(x)
     if out.shape != x.shape or out.dtype != torch.bfloat16 or not out.is_contiguous():
         raise ValueError("out must be a contiguous bf16 tensor shaped like x")
+    nbytes = ctypes.c_size_t(0)
+    _lib.call("npub200_group_norm_scratch_size", n, int(groups), ctypes.byref(nbytes))
     key = (x.device.index or 0, torch.cuda.current_stream(x.device).cuda_stream)
     st = _GN_STATS.get(key)
-    if st is None or st.numel() < 2 * n * groups:
-        st = torch.empty(max(2 * n * groups, 4096), dtype=torch.float32, device=x.device)
+    if st is None or st.numel() * 4 < nbytes.value:
+        # zeroed once: the scratch ends in ticket counters the kernels leave zero
+        st = torch.zeros(max(nbytes.value // 4 + 1, 1 << 16), dtype=torch.float32, device=x.device)
         _GN_STATS[key] = st
     with torch.cuda.device(x.device):
         _lib.call("npub200_group_norm", ctypes.c_void_p(x.data_ptr()), n, h * w, c, int(groups),

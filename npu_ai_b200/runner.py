@@ -255,7 +255,7 @@ class NpuGemm:
         return b.contiguous()
 
     def matmul_t(self, x, w: NpuWeight, bias=None, out: torch.Tensor | None = None,
-                 out_dtype: torch.dtype | None = None) -> torch.Tensor:
+                 out_dtype: torch.dtype | None = None, residual: torch.Tensor | None = None) -> torch.Tensor:
         """x: (M, K) numpy/torch float -> (M, N) CUDA tensor = x @ W (+ bias); bf16 operands, f32 accumulation,
         bias in f32 (npu/xdna1_gemm.py:349-422). f32 output unless `out_dtype`/`out` say otherwise."""
         t_start = time.perf_counter()
@@ -266,7 +266,7 @@ class NpuGemm:
         assert K == w.K, f"K mismatch: x has {K}, weight has {w.K}"
         ev = self._events()
         y = kernels.gemm(x2, w.tensor[:, :K] if w.handle is None else w.tensor, self._bias_device(bias), out=out,
-                         out_dtype=out_dtype or self.out_dtype, handle=w.handle)
+                         out_dtype=out_dtype or self.out_dtype, handle=w.handle, residual=residual)
         self._close("gemm", ev)
         with self._lock:
             self.stats["calls"] += 1
@@ -279,14 +279,16 @@ class NpuGemm:
         """x: (M, K) -> (M, N) float32 numpy array (copied back to the host)."""
         return self.matmul_t(x, w, out_dtype=torch.float32).cpu().numpy()
 
-    def linear(self, x, w: NpuWeight, bias=None, out_dtype: torch.dtype | None = None):
-        """x: (..., K) -> (..., N) = x @ W (+ bias). torch in -> torch (CUDA) out, numpy in -> numpy out
-        (npu/xdna1_gemm.py:428-448)."""
+    def linear(self, x, w: NpuWeight, bias=None, out_dtype: torch.dtype | None = None,
+               residual: torch.Tensor | None = None):
+        """x: (..., K) -> (..., N) = x @ W (+ bias) (+ residual, a bf16 (..., N) CUDA tensor added in the GEMM's
+        epilogue). torch in -> torch (CUDA) out, numpy in -> numpy out (npu/xdna1_gemm.py:428-448)."""
         is_torch = isinstance(x, torch.Tensor)
         xt = _as_tensor(x)
         shp = tuple(xt.shape)
         x2 = xt.reshape(-1, shp[-1])
-        y = self.matmul_t(x2, w, bias, out_dtype=out_dtype).view(*shp[:-1], w.N)
+        r2 = residual.reshape(-1, w.N) if residual is not None else None
+        y = self.matmul_t(x2, w, bias, out_dtype=out_dtype, residual=r2).view(*shp[:-1], w.N)
         return y if is_torch else y.cpu().numpy()
 
     def linear_geglu(self, x, w: NpuWeight, bias=None, out_dtype: torch.dtype | None = None) -> torch.Tensor:

@@ -185,3 +185,24 @@ def test_repack_then_split_k_share_workspace(cuda_device):
     for MKN in [(100, 100, 100), (154, 768, 320), (99, 1001, 77), (512, 1280, 1280), (77, 5120, 1280)]:
         x, w, b = _inputs(*MKN, seed=sum(MKN))
         _check_f32(_run(x, w, b), linear_ref(x, w, b))
+
+
+@pytest.mark.parametrize("shape", [(4096, 320, 320), (77, 5120, 1280), (300, 640, 200)],
+                         ids=["to_out", "splitK", "ragged"])
+def test_gemm_residual_epilogue(cuda_device, shape):
+    """out = x W^T + b + residual in one kernel (a transformer block's residual connection), also in place (the
+    residual buffer receives the result) and on a split-K shape, where the reducing split adds it."""
+    from npu_ai_b200 import kernels
+    dev = torch.device("cuda", 0)
+    M, K, N = shape
+    x, w, b = _inputs(M, K, N, seed=M + K + 11)
+    r = torch.randn(M, N, generator=torch.Generator().manual_seed(12)).to(torch.bfloat16)
+    ref = linear_ref(x, w, b) + r.float()
+    xd, wd, bd = x.to(dev), w.to(dev), b.to(dev)
+    y = kernels.gemm(xd, wd, bd, out_dtype=torch.float32, residual=r.to(dev))
+    kernels.check_status(dev)
+    _check_f32(y, ref)
+    rd = r.to(dev).clone()
+    kernels.gemm(xd, wd, bd, out=rd, residual=rd)
+    kernels.check_status(dev)
+    _check_bf16(rd, ref)
