@@ -37,15 +37,23 @@ __global__ void __launch_bounds__(kStatsThreads)
   const int p_end = int((long long)hw * (slice + 1) / slices);
   const __nv_bfloat16* base = x + (long long)img * hw * c + (long long)g * cg;
   float s = 0.f, ss = 0.f;
-  if ((cg & 1) == 0) {
-    // channel pairs (c and cg even, so the group's first channel is even)
+  if ((cg & 1) == 0 && cg / 2 <= kStatsThreads) {
+    // Each thread keeps one channel pair of the group and strides over pixels (no per-element index division);
+    // the threads of a pixel row read its contiguous cg-channel segment.
     const int pairs = cg / 2;
-    for (int i = p_begin * pairs + threadIdx.x; i < p_end * pairs; i += kStatsThreads) {
-      const int p = i / pairs;
-      const int k = i - p * pairs;
-      const float2 v = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(base + (long long)p * c)[k]);
-      s += v.x + v.y;
-      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, ss));
+    const int rows = kStatsThreads / pairs;  // pixel rows per pass
+    const int k = threadIdx.x % pairs;
+    const int r = threadIdx.x / pairs;
+    if (r < rows) {
+      const __nv_bfloat162* col = reinterpret_cast<const __nv_bfloat162*>(base) + k;
+      const long long step = (long long)rows * c / 2;  // bf16 pairs between passes
+      const __nv_bfloat162* ptr = col + (long long)(p_begin + r) * c / 2;
+#pragma unroll 4
+      for (int p = p_begin + r; p < p_end; p += rows, ptr += step) {  // unrolled: several loads in flight
+        const float2 v = __bfloat1622float2(*ptr);
+        s += v.x + v.y;
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, ss));
+      }
     }
   } else {
     for (int i = p_begin * cg + threadIdx.x; i < p_end * cg; i += kStatsThreads) {
@@ -97,34 +105,46 @@ __global__ void __launch_bounds__(kStatsThreads)
 
 __device__ __forceinline__ float silu(float v) { return v / (1.0f + __expf(-v)); }
 
+constexpr int kApplyThreads = 256;
+
+// y = act(x * A[ch] + B[ch]) with A = rstd * gamma, B = beta - mean * A for this image: the block builds the table
+// for its image's channels in shared memory, then streams its pixels 8 channels (16 bytes) per thread.
 // x and y may be the same tensor (each element is read and written by one thread), so neither is __restrict__.
-__global__ void gn_apply_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, long long pixels,
-                                int hw, int c, int cg, int groups, const float2* __restrict__ stats,
-                                const float* __restrict__ gamma, const float* __restrict__ beta, int apply_silu) {
+__global__ void __launch_bounds__(kApplyThreads)
+    gn_apply_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, int hw, int c, int cg, int groups, int block_pixels,
+                    const float2* __restrict__ stats, const float* __restrict__ gamma,
+                    const float* __restrict__ beta, int apply_silu) {
+  extern __shared__ float2 ab[];  // [c]: (A, B)
+  const int img = blockIdx.y;
+  for (int ch = threadIdx.x; ch < c; ch += kApplyThreads) {
+    const float2 st = stats[img * groups + ch / cg];
+    const float a = st.y * gamma[ch];
+    ab[ch] = make_float2(a, beta[ch] - st.x * a);
+  }
+  __syncthreads();
   const int chunks = c / 8;
-  const long long total = pixels * chunks;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long p = i / chunks;
-    const int c0 = int(i - p * chunks) * 8;
-    const int img = int(p / hw);
-    const uint4 raw = *reinterpret_cast<const uint4*>(x + p * c + c0);
+  const int p0 = blockIdx.x * block_pixels;
+  const int np = min(block_pixels, hw - p0);
+  const long long base = ((long long)img * hw + p0) * c;
+  for (int i = threadIdx.x; i < np * chunks; i += kApplyThreads) {
+    const int p = i / chunks;  // one division per 8 values
+    const int c0 = (i - p * chunks) * 8;
+    const long long off = base + (long long)p * c + c0;
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + off);
     const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
     uint32_t o[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float v[2] = {__uint_as_float(w[e] << 16), __uint_as_float(w[e] & 0xFFFF0000u)};
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int ch = c0 + 2 * e + t;
-        const float2 st = stats[img * groups + ch / cg];
-        float r = (v[t] - st.x) * st.y * gamma[ch] + beta[ch];
-        if (apply_silu) r = silu(r);
-        v[t] = r;
+      const float2 ab0 = ab[c0 + 2 * e], ab1 = ab[c0 + 2 * e + 1];
+      float v0 = fmaf(__uint_as_float(w[e] << 16), ab0.x, ab0.y);
+      float v1 = fmaf(__uint_as_float(w[e] & 0xFFFF0000u), ab1.x, ab1.y);
+      if (apply_silu) {
+        v0 = __fdividef(v0, 1.0f + __expf(-v0));
+        v1 = __fdividef(v1, 1.0f + __expf(-v1));
       }
-      o[e] = pack_bf16x2(v[0], v[1]);
+      o[e] = pack_bf16x2(v0, v1);
     }
-    *reinterpret_cast<uint4*>(y + p * c + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(y + off) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -161,12 +181,15 @@ int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t g
       static_cast<const __nv_bfloat16*>(x), int(hw), int(c), int(cg), eps, reinterpret_cast<float2*>(st),
       reinterpret_cast<float2*>(partials), counters);
   if (int rc = check_cuda(cudaGetLastError(), "group_norm stats launch")) return rc;
-  const long long total = n * hw * (c / 8);
-  const int threads = 256;
-  const int grid = int(std::min<long long>((total + threads - 1) / threads, (long long)dev->sms * 16));
-  gn_apply_kernel<<<grid, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out),
-                                                n * hw, int(hw), int(c), int(c / groups), int(groups),
-                                                reinterpret_cast<const float2*>(st), gamma, beta, apply_silu);
+  if (c > 6144) return fail(kErrUnsupported, "group_norm: at most 6144 channels");  // 48 KB scale/shift table
+  // Pixels per apply block (within one image): about four blocks per SM over the whole tensor, at least one pixel.
+  const int64_t vecs = n * hw * (c / 8);
+  const int64_t per_block = (vecs + int64_t(dev->sms) * 4 - 1) / (int64_t(dev->sms) * 4);
+  const int64_t block_pixels = std::max<int64_t>(1, std::min<int64_t>(hw, (per_block + c / 8 - 1) / (c / 8)));
+  const dim3 agrid(unsigned((hw + block_pixels - 1) / block_pixels), unsigned(n));
+  gn_apply_kernel<<<agrid, kApplyThreads, size_t(c) * sizeof(float2), stream>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), int(hw), int(c), int(c / groups),
+      int(groups), int(block_pixels), reinterpret_cast<const float2*>(st), gamma, beta, apply_silu);
   return check_cuda(cudaGetLastError(), "group_norm apply launch");
 }
 
