@@ -651,6 +651,7 @@ def run_case(args) -> None:
     device = torch.device("cuda", 0)
     kind, dims = args.case.split(":")
     d = [int(t) for t in dims.split(",")]
+    gn_bytes = 0.0
     if kind == "gemm":
         M, K, N = d
         x, w, b = _seeded((M, K), 1.0, 1, device), _seeded((N, K), 0.02, 2, device), _seeded((N,), 0.01, 3, device)
@@ -661,8 +662,29 @@ def run_case(args) -> None:
         q, k, v = (_seeded((B, S, H * D), 1.0, i, device) for i, S in ((1, Sq), (2, Skv), (3, Skv)))
         out = torch.empty((B, Sq, H * D), dtype=torch.bfloat16, device=device)
         fn, flops = (lambda: kernels.attention(q, k, v, H, out=out)), 4.0 * B * H * Sq * Skv * D
+    elif kind == "geglu":
+        M, K, n = d
+        x, w, b = _seeded((M, K), 1.0, 1, device), _seeded((2 * n, K), 0.05, 2, device), _seeded((2 * n,), 0.1, 3, device)
+        out = torch.empty((M, n), dtype=torch.bfloat16, device=device)
+        fn, flops = (lambda: kernels.gemm_geglu(x, w, b, out=out)), 2.0 * M * K * 2 * n
+    elif kind == "conv":
+        n, h, w_, cin, cout = d
+        x = _seeded((n, h, w_, cin), 1.0, 1, device)
+        wp = kernels.pack_conv3x3_weight(_seeded((cout, cin, 3, 3), (9 * cin) ** -0.5, 2, device))
+        b = _seeded((cout,), 0.1, 3, device).float()
+        out = torch.empty((n, h, w_, cout), dtype=torch.bfloat16, device=device)
+        fn, flops = (lambda: kernels.conv3x3(x, wp, b, out=out)), 2.0 * n * h * w_ * cout * 9 * cin
+    elif kind == "gn":
+        n, h, w_, c = d
+        x = _seeded((n, h, w_, c), 1.0, 1, device)
+        g, bb = torch.ones(c, device=device), torch.zeros(c, device=device)
+        out = torch.empty_like(x)
+        # bytes, not FLOPs: one read for the statistics, one read and one write for the apply pass
+        fn, flops = (lambda: kernels.group_norm(x, 32, g, bb, silu=True, out=out)), 0.0
+        gn_bytes = 3.0 * x.numel() * 2
     else:
-        raise SystemExit(f"unknown case kind {kind!r} (gemm:M,K,N or attn:B,H,Sq,Skv,D)")
+        raise SystemExit(f"unknown case kind {kind!r} (gemm:M,K,N, attn:B,H,Sq,Skv,D, geglu:M,K,n, "
+                         "conv:n,h,w,cin,cout or gn:n,h,w,c)")
     for _ in range(args.warmup):
         fn()
     torch.cuda.synchronize()
@@ -675,7 +697,8 @@ def run_case(args) -> None:
     kernels.check_status(device)
     ms = e0.elapsed_time(e1) / args.steps
     print(json.dumps({"case": args.case, "us_per_launch": round(ms * 1e3, 2),
-                      "tflops": round(flops / ms / 1e9, 1)}), flush=True)
+                      "tflops": round(flops / ms / 1e9, 1),
+                      **({"gbs": round(gn_bytes / ms / 1e6, 1)} if kind == "gn" else {})}), flush=True)
 
 
 def main(argv=None) -> int:
@@ -686,7 +709,8 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
-    ap.add_argument("--case", default=None, help="time one kernel: gemm:M,K,N or attn:B,H,Sq,Skv,D")
+    ap.add_argument("--case", default=None, help="time one kernel: gemm:M,K,N, attn:B,H,Sq,Skv,D, geglu:M,K,n, "
+                                                   "conv:n,h,w,cin,cout or gn:n,h,w,c")
     ap.add_argument("--workload", choices=["hotpath", "unet"], default="hotpath",
                     help="hotpath: the GEMM sweep + attention blocks (default); unet: SD1.5 UNet denoise steps")
     ap.add_argument("--batch", type=int, default=2, help="unet: images per step, both CFG halves (2 = 1 prompt)")

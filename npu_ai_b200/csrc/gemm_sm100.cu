@@ -183,8 +183,21 @@ constexpr int kModePlain = 0;
 constexpr int kModeGeglu = 1;
 constexpr int kModeConv3x3 = 2;
 
-// GELU with the error function (torch's default `F.gelu`, approximate='none').
-__device__ __forceinline__ float gelu_erf(float y) { return 0.5f * y * (1.0f + erff(y * 0.70710678118654752f)); }
+// GELU with the error function (torch's default `F.gelu`, approximate='none'): y * Phi(y) = y/2 * (1 + erf(y/sqrt2)).
+// erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26 (Hastings' rational approximation,
+// |error| <= 1.5e-7): for z >= 0, erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2), t = 1 / (1 + p z).
+// One reciprocal and one exp2 on the MUFU and a handful of FMAs, so the gating keeps up with the main loop. For
+// y < 0 the factor 1 + erf = t (...) exp(-z^2) is taken directly, without cancelling against 1.
+__device__ __forceinline__ float gelu_erf(float y) {
+  const float z = fabsf(y) * 0.70710678118654752f;
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+  float q = fmaf(1.061405429f, t, -1.453152027f);
+  q = fmaf(q, t, 1.421413741f);
+  q = fmaf(q, t, -0.284496736f);
+  q = fmaf(q, t, 0.254829592f);
+  const float tail = q * t * fast_exp2(-z * z * 1.4426950408889634f);  // 1 - erf(z)
+  return 0.5f * y * (y >= 0.0f ? 2.0f - tail : tail);
+}
 
 __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& m_blk, int& n_blk) {
   if (a.n_fastest) {
