@@ -70,9 +70,12 @@ struct GemmLayout {
   static constexpr int kStagingOffset = STAGES * kStageBytes;
   static constexpr int kStagingBytes = 4 * 2 * 32 * 128;
   static constexpr int kBarOffset = kStagingOffset + kStagingBytes;
-  static constexpr int kNumBars = 2 * STAGES + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], drain
+  // full[S], empty[S], acc_full[2], acc_empty[2], drain, bias_full, bias_free
+  static constexpr int kNumBars = 2 * STAGES + 7;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
-  static constexpr int kSmemBytes = kMiscOffset + 16 + 1024;  // + slack to align the base to 1 KB
+  // The tile's bias in f32 (BN entries: the output columns', then in the GEGLU form the gate columns').
+  static constexpr int kBiasOffset = (kMiscOffset + 16 + 15) / 16 * 16;
+  static constexpr int kSmemBytes = kBiasOffset + BN * 4 + 1024;  // + slack to align the base to 1 KB
   static_assert(kBBytes % 1024 == 0, "B stage must keep 1 KB alignment for the 128-byte swizzle");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "N tile: a multiple of 32 (UMMA N for M=128 <= 256)");
   static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
@@ -252,6 +255,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* acc_full = bars + 2 * STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
+  uint64_t* bias_full = drain + 1;  // the epilogue warps have written this tile's bias table
+  uint64_t* bias_free = drain + 2;  // the epilogue warps are done reading the previous tile's table
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
 
@@ -268,6 +273,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
+    mbar_init(bias_full, 128);  // one arrival per epilogue thread
+    mbar_init(bias_free, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -423,6 +430,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int splits = args.splits;
     int chunk_no = 0;
     int local = 0;
+    // One bias row for the whole output: read from a per-tile table in shared memory. A bias row per image is read
+    // by each thread for its own row.
+    const bool table_bias = args.bias != nullptr && args.bias_img_stride == 0;
+    float* bias_tab = reinterpret_cast<float*>(smem + L::kBiasOffset);
     pdl_wait();  // the previous kernel may still read (or write) the output / bias
     for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -439,14 +450,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           prefetch_l2(static_cast<const uint8_t*>(args.bias) + (size_t(args.N) + size_t(pnb) * kOutCols) * esz +
                       lane * 128);
       }
-      if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.ctl, kStatusTimeoutEpilogue)) break;
-      tc_fence_after();
       const int tile = unit / splits;
       const int split = unit % splits;
       int mb, nb;
       tile_coords(args, tile, mb, nb);
       const int m0 = mb * kGemmBM;
       const int n0 = nb * kOutCols;
+      if (table_bias) {
+        // This tile's bias table: each epilogue thread fetches up to two entries (requested before any wait),
+        // stores them once every warp is done with the previous tile's table, then all wait for the full table.
+        const int t = int(threadIdx.x) - 64;
+        float e[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int i = t + 128 * k;
+          const int col = i < kOutCols ? n0 + i : args.N + n0 + (i - kOutCols);
+          e[k] = (i < BN && col < args.bias_n)
+                     ? (args.bias_f32 ? __ldg(static_cast<const float*>(args.bias) + col)
+                                      : __bfloat162float(static_cast<const __nv_bfloat16*>(args.bias)[col]))
+                     : 0.0f;
+        }
+        if (local > 0 &&
+            !mbar_wait_bounded(bias_free, uint32_t(local - 1) & 1u, abort_flag, args.ctl, kStatusTimeoutEpilogue))
+          break;
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+          if (t + 128 * k < BN) bias_tab[t + 128 * k] = e[k];
+        mbar_arrive(bias_full);
+        if (!mbar_wait_bounded(bias_full, uint32_t(local) & 1u, abort_flag, args.ctl, kStatusTimeoutEpilogue)) break;
+      }
+      if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.ctl, kStatusTimeoutEpilogue)) break;
+      tc_fence_after();
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
       bool emit = true;
       if (!GEGLU && splits > 1) {
@@ -484,16 +518,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint32_t r[32];
             tmem_ld32(t_row + uint32_t(c), r);
             float b[32];
-            long long bias_row = 0;
-            if (args.bias_img_stride > 0)
-              bias_row = (long long)min((m0 + row) / args.bias_img_pixels, args.bias_imgs - 1) * args.bias_img_stride;
-            load_bias32(args, n0 + c, b, bias_row);
+            if (table_bias) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 t4 = reinterpret_cast<const float4*>(bias_tab + c)[j];
+                b[4 * j] = t4.x;
+                b[4 * j + 1] = t4.y;
+                b[4 * j + 2] = t4.z;
+                b[4 * j + 3] = t4.w;
+              }
+            } else {
+              long long bias_row = 0;
+              if (args.bias_img_stride > 0)
+                bias_row =
+                    (long long)min((m0 + row) / args.bias_img_pixels, args.bias_imgs - 1) * args.bias_img_stride;
+              load_bias32(args, n0 + c, b, bias_row);
+            }
             float v[32];
             if constexpr (GEGLU) {
               uint32_t rg[32];
               tmem_ld32(t_row + uint32_t(kOutCols + c), rg);
               float bg[32];
-              load_bias32(args, args.N + n0 + c, bg);
+              if (table_bias) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float4 t4 = reinterpret_cast<const float4*>(bias_tab + kOutCols + c)[j];
+                  bg[4 * j] = t4.x;
+                  bg[4 * j + 1] = t4.y;
+                  bg[4 * j + 2] = t4.z;
+                  bg[4 * j + 3] = t4.w;
+                }
+              } else {
+                load_bias32(args, args.N + n0 + c, bg);
+              }
               tmem_wait_ld();
 #pragma unroll
               for (int j = 0; j < 32; ++j)
@@ -581,6 +638,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (table_bias) mbar_arrive(bias_free);
     }
     if (args.tma_store && lane == 0) bulk_wait_read<0>();  // staging must not be released while being read
   }
