@@ -33,7 +33,12 @@ namespace npub200 {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle atom of bf16 along K
-constexpr int kGemmThreads = 192;
+// Warp roles: 0 = TMA producer, 1 = MMA issuer, 2..9 = epilogue. Two epilogue warps share each TMEM lane quarter
+// (32 accumulator rows) and take alternate output chunks, so one warp's TMEM-load and store latencies overlap the
+// other's arithmetic.
+constexpr int kGemmEpiWarps = 8;
+constexpr int kGemmEpiThreads = kGemmEpiWarps * 32;
+constexpr int kGemmThreads = 64 + kGemmEpiThreads;
 
 struct GemmArgs {
   int M, N, K;
@@ -66,9 +71,9 @@ struct GemmLayout {
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  // Epilogue staging: per epilogue warp two 32-row x 128-byte tiles (128-byte swizzle) for the TMA stores.
+  // Epilogue staging: per epilogue warp one 32-row x 128-byte tile (128-byte swizzle) for the TMA stores.
   static constexpr int kStagingOffset = STAGES * kStageBytes;
-  static constexpr int kStagingBytes = 4 * 2 * 32 * 128;
+  static constexpr int kStagingBytes = kGemmEpiWarps * 32 * 128;
   static constexpr int kBarOffset = kStagingOffset + kStagingBytes;
   // full[S], empty[S], acc_full[2], acc_empty[2], drain, bias_full, bias_free
   static constexpr int kNumBars = 2 * STAGES + 7;
@@ -270,11 +275,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[a], kGemmEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
-    mbar_init(bias_full, 128);  // one arrival per epilogue thread
-    mbar_init(bias_free, 128);
+    mbar_init(bias_full, kGemmEpiThreads);  // one arrival per epilogue thread
+    mbar_init(bias_free, kGemmEpiThreads);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -294,7 +299,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   pdl_launch_dependents();
 
   const int num_units = args.num_tiles * args.splits;
-  const int num_m = args.num_m_blk;
   const int num_kb = args.num_kb;
 
   if (warp == 0) {
@@ -418,17 +422,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_wait_drain(drain, 0u, args.ctl);
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------------------------ epilogue (warps 2..9)
     const int quarter = warp & 3;  // TMEM lanes this warp may access: [32*quarter, 32*quarter + 32)
+    const int half = (warp - 2) >> 2;  // which of the quarter's two warps: output chunks half, half + 2, ...
     const int row = quarter * 32 + lane;
-    // Output goes out in chunks of 128-byte rows (64 bf16 or 32 f32 columns) through a double-buffered staging
-    // tile per warp, laid out with the 128-byte swizzle so the row-per-thread writes hit distinct banks. A chunk
-    // that would reach past the tile (BN not a multiple of the chunk) is written with direct stores instead.
-    uint8_t* staging = smem + L::kStagingOffset + (warp - 2) * (2 * 32 * 128);
+    // Output goes out in chunks of 128-byte rows (64 bf16 or 32 f32 columns) through a staging tile per warp,
+    // laid out with the 128-byte swizzle so the row-per-thread writes hit distinct banks; the quarter's two warps
+    // alternate chunks. A chunk that would reach past the tile (BN not a multiple of the chunk) is written with
+    // direct stores instead.
+    uint8_t* sb = smem + L::kStagingOffset + (warp - 2) * (32 * 128);
     volatile int* last_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 8);
     const int cw = args.out_f32 ? 32 : 64;
     const int splits = args.splits;
-    int chunk_no = 0;
     int local = 0;
     // One bias row for the whole output: read from a per-tile table in shared memory. A bias row per image is read
     // by each thread for its own row.
@@ -459,23 +464,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (table_bias) {
         // This tile's bias table: each epilogue thread fetches up to two entries (requested before any wait),
         // stores them once every warp is done with the previous tile's table, then all wait for the full table.
-        const int t = int(threadIdx.x) - 64;
-        float e[2];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int i = t + 128 * k;
-          const int col = i < kOutCols ? n0 + i : args.N + n0 + (i - kOutCols);
-          e[k] = (i < BN && col < args.bias_n)
-                     ? (args.bias_f32 ? __ldg(static_cast<const float*>(args.bias) + col)
-                                      : __bfloat162float(static_cast<const __nv_bfloat16*>(args.bias)[col]))
-                     : 0.0f;
-        }
+        static_assert(BN <= kGemmEpiThreads, "one bias table entry per epilogue thread");
+        const int i = int(threadIdx.x) - 64;
+        const int col = i < kOutCols ? n0 + i : args.N + n0 + (i - kOutCols);
+        const float e = (i < BN && col < args.bias_n)
+                            ? (args.bias_f32 ? __ldg(static_cast<const float*>(args.bias) + col)
+                                             : __bfloat162float(static_cast<const __nv_bfloat16*>(args.bias)[col]))
+                            : 0.0f;
         if (local > 0 &&
             !mbar_wait_bounded(bias_free, uint32_t(local - 1) & 1u, abort_flag, args.ctl, kStatusTimeoutEpilogue))
           break;
-#pragma unroll
-        for (int k = 0; k < 2; ++k)
-          if (t + 128 * k < BN) bias_tab[t + 128 * k] = e[k];
+        if (i < BN) bias_tab[i] = e;
         mbar_arrive(bias_full);
         if (!mbar_wait_bounded(bias_full, uint32_t(local) & 1u, abort_flag, args.ctl, kStatusTimeoutEpilogue)) break;
       }
@@ -487,7 +486,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // Publish this split's partial, then take a ticket; the last split of the tile reduces.
         float* mine = args.ws_partial + (size_t(tile) * splits + split) * BN * kGemmBM;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = half * 32; c < BN; c += 64) {
           uint32_t r[32];
           tmem_ld32(t_row + uint32_t(c), r);
           tmem_wait_ld();
@@ -495,71 +494,64 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int j = 0; j < 32; ++j) __stcg(mine + (c + j) * kGemmBM + row, __uint_as_float(r[j]));
         }
         __threadfence();
-        named_barrier_sync(1, 128);
+        named_barrier_sync(1, kGemmEpiThreads);
         if (threadIdx.x == 64) {
           const unsigned int ticket = atomicAdd(args.ws_counter + tile, 1u);
           *last_flag = (ticket == unsigned(splits - 1)) ? 1 : 0;
         }
-        named_barrier_sync(1, 128);
+        named_barrier_sync(1, kGemmEpiThreads);
         emit = *last_flag != 0;
         __threadfence();
       }
       if (emit) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < kOutCols; c0 += cw) {
+        for (int c0 = half * cw; c0 < kOutCols; c0 += 2 * cw) {
           const bool chunk_tma = args.tma_store && c0 + cw <= kOutCols;
-          uint8_t* sb = staging + (chunk_no & 1) * (32 * 128);
           if (chunk_tma) {
-            if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
+            if (lane == 0) bulk_wait_read<0>();  // this warp's previous store has read the staging tile
             __syncwarp();
           }
 #pragma unroll 1
           for (int c = c0; c < min(c0 + cw, kOutCols); c += 32) {
-            uint32_t r[32];
-            tmem_ld32(t_row + uint32_t(c), r);
-            float b[32];
-            if (table_bias) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 t4 = reinterpret_cast<const float4*>(bias_tab + c)[j];
-                b[4 * j] = t4.x;
-                b[4 * j + 1] = t4.y;
-                b[4 * j + 2] = t4.z;
-                b[4 * j + 3] = t4.w;
-              }
-            } else {
-              long long bias_row = 0;
-              if (args.bias_img_stride > 0)
-                bias_row =
-                    (long long)min((m0 + row) / args.bias_img_pixels, args.bias_imgs - 1) * args.bias_img_stride;
-              load_bias32(args, n0 + c, b, bias_row);
-            }
-            float v[32];
-            if constexpr (GEGLU) {
-              uint32_t rg[32];
-              tmem_ld32(t_row + uint32_t(kOutCols + c), rg);
-              float bg[32];
+            // Bias of the 32 columns from column offset `off` of the tile (the table) or of the output (own row).
+            auto fetch_bias = [&](float (&bb)[32], int off, int gcol) {
               if (table_bias) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                  const float4 t4 = reinterpret_cast<const float4*>(bias_tab + kOutCols + c)[j];
-                  bg[4 * j] = t4.x;
-                  bg[4 * j + 1] = t4.y;
-                  bg[4 * j + 2] = t4.z;
-                  bg[4 * j + 3] = t4.w;
+                  const float4 t4 = reinterpret_cast<const float4*>(bias_tab + off)[j];
+                  bb[4 * j] = t4.x;
+                  bb[4 * j + 1] = t4.y;
+                  bb[4 * j + 2] = t4.z;
+                  bb[4 * j + 3] = t4.w;
                 }
               } else {
-                load_bias32(args, args.N + n0 + c, bg);
+                long long bias_row = 0;
+                if (args.bias_img_stride > 0)
+                  bias_row =
+                      (long long)min((m0 + row) / args.bias_img_pixels, args.bias_imgs - 1) * args.bias_img_stride;
+                load_bias32(args, gcol, bb, bias_row);
+              }
+            };
+            float v[32];
+            if constexpr (GEGLU) {
+              uint32_t r[32], rg[32];
+              tmem_ld32(t_row + uint32_t(c), r);
+              tmem_ld32(t_row + uint32_t(kOutCols + c), rg);
+              float b[32], bg[32];
+              fetch_bias(b, c, n0 + c);
+              if (table_bias) {
+                fetch_bias(bg, kOutCols + c, 0);
+              } else {
+                load_bias32(args, args.N + n0 + c, bg);  // gate columns: one bias row
               }
               tmem_wait_ld();
 #pragma unroll
               for (int j = 0; j < 32; ++j)
                 v[j] = (__uint_as_float(r[j]) + b[j]) * gelu_erf(__uint_as_float(rg[j]) + bg[j]);
             } else {
-              tmem_wait_ld();
               if (splits > 1) {
-                // Fixed summation order over the splits, this split's own partial taken from TMEM. The partials
-                // sit in L2 and each pass costs a round trip there, so two splits' loads go out per pass.
+                // Fixed summation order over the splits, every partial (this split's own too, published above)
+                // read back from L2. Each pass costs a round trip there, so two splits' loads go out per pass.
                 const float* part0 = args.ws_partial + size_t(tile) * splits * BN * kGemmBM + c * kGemmBM + row;
                 const size_t slab = size_t(BN) * kGemmBM;
 #pragma unroll
@@ -568,17 +560,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int sp = 0; sp < splits; sp += 2) {
                   float p0[32], p1[32];
                   const bool two = sp + 1 < splits;
-                  if (sp == split) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) p0[j] = __uint_as_float(r[j]);
-                  } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) p0[j] = __ldcg(part0 + sp * slab + j * kGemmBM);
-                  }
-                  if (two && sp + 1 == split) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) p1[j] = __uint_as_float(r[j]);
-                  } else if (two) {
+                  for (int j = 0; j < 32; ++j) p0[j] = __ldcg(part0 + sp * slab + j * kGemmBM);
+                  if (two) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) p1[j] = __ldcg(part0 + (sp + 1) * slab + j * kGemmBM);
                   }
@@ -589,12 +573,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     for (int j = 0; j < 32; ++j) v[j] += p1[j];
                   }
                 }
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] += b[j];
               } else {
+                uint32_t r[32];
+                tmem_ld32(t_row + uint32_t(c), r);
+                tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + b[j];
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
               }
+              float b[32];
+              fetch_bias(b, c, n0 + c);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += b[j];
               if (args.residual != nullptr) add_residual32(args, m0 + row, n0 + c, v);
             }
             if (chunk_tma) {
@@ -630,7 +619,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               tma_store_2d(&tm_out, sb, n0 + c0, m0 + quarter * 32);
               bulk_commit();
             }
-            ++chunk_no;
           }
         }
         if (!GEGLU && splits > 1 && threadIdx.x == 64) args.ws_counter[tile] = 0u;  // leave the counter zeroed for reuse
@@ -724,8 +712,8 @@ constexpr size_t kSplitCounterBytes = 4096;
 // Modelled time (SM clocks) of a plan: waves of persistent work units x per-unit time. A unit's main loop is
 // bounded by the larger of the tensor-core time (2*BN clocks per 64-deep K block at 8192 FLOP/clk/SM) and the
 // time to stream its operands into shared memory (~64 B/clk/SM); each unit pays a fixed pipeline fill. A split
-// tile pays for publishing its f32 partial and for the last split's reduction, which is latency-bound: per
-// 32-column chunk one L2 round trip (~1050 clocks measured) per two splits.
+// tile pays for publishing its f32 partial and for the last split's reduction, which is latency-bound: each
+// epilogue warp reduces BN/64 groups of 32 columns, one L2 round trip (~1050 clocks measured) per two splits.
 double plan_cost(int64_t M, int64_t N, int64_t kb, int bn, int splits, int sms) {
   const int64_t tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + bn - 1) / bn);
   const int64_t units = tiles * splits;
@@ -734,7 +722,7 @@ double plan_cost(int64_t M, int64_t N, int64_t kb, int bn, int splits, int sms) 
   const double mma = 2.0 * bn;
   const double load = (kGemmBM + bn) * 128.0 / 64.0;
   double t = double(kb_unit) * std::max(mma, load) + 1500.0 + 8.0 * bn;
-  if (splits > 1) t += 1000.0 + (bn / 32.0) * (300.0 + 1050.0 * double((splits + 1) / 2));
+  if (splits > 1) t += 1000.0 + (bn / 64.0) * (600.0 + 1050.0 * double((splits + 1) / 2));
   return double(waves) * t;
 }
 }  // namespace

@@ -103,7 +103,6 @@ __global__ void __launch_bounds__(kStatsThreads)
   }
 }
 
-__device__ __forceinline__ float silu(float v) { return v / (1.0f + __expf(-v)); }
 
 constexpr int kApplyThreads = 256;
 
