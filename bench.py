@@ -524,7 +524,7 @@ def run_e2e(args, dist, device, total_flops) -> dict:
 
 
 # ----------------------------------------------------------------------------------------------------------------
-# UNet workload: SD1.5-architecture UNet denoise steps (BASELINE configs 3 and 4)
+# UNet workload: SD1.5-architecture UNet denoise steps (batch 2 with 4 Euler steps; batch 16, sharded over GPUs)
 # ----------------------------------------------------------------------------------------------------------------
 def run_unet(args, dist) -> None:
     """Euler CFG denoise steps of a random-init SD1.5-architecture UNet with every Linear and attention on the B200

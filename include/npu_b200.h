@@ -71,8 +71,9 @@ int npub200_gemm_workspace_size(const void* x, int64_t ldx, int64_t m, int64_t k
 int npub200_gemm(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
                  const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype, void* workspace,
                  size_t workspace_bytes, int variant, void* stream);
-/* The launch plan the library picks for a GEMM shape on the current device: N tile and split-K factor
- * (the B200 counterpart of NpuGemm.dispatch_shapes, npu/xdna1_gemm.py:295-297, which lists the padded chunks). */
+/* The launch plan the library picks for a GEMM shape on the current device: tile variant (N tile, or 1000 + N tile
+ * for 256-row tiles on a two-CTA cluster) and split-K factor (the B200 counterpart of NpuGemm.dispatch_shapes,
+ * npu/xdna1_gemm.py:295-297, which lists the padded chunks). */
 int npub200_gemm_plan(int64_t m, int64_t n, int64_t k, int variant, int* tile_n_out, int* splits_out);
 /* Same with a registered weight (the resident-weight path the runner uses). */
 int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t weight, const void* bias,

@@ -305,7 +305,7 @@ int npub200_gemm_plan(int64_t m, int64_t n, int64_t k, int variant, int* tile_n_
   const DeviceInfo* d = nullptr;
   if (int rc = current_device_info(&d)) return rc;
   const GemmPlan plan = gemm_plan(m, n, round_up(k, 8), d->sms, variant);
-  if (tile_n_out) *tile_n_out = plan.bn;
+  if (tile_n_out) *tile_n_out = gemm_plan_variant(plan);
   if (splits_out) *splits_out = plan.splits;
   return kOk;
 }
@@ -412,16 +412,17 @@ int npub200_gemm_w(const void* x, int64_t ldx, int64_t m, int64_t k, int64_t wei
     if (int rc = current_device_info(&d)) return rc;
     if (d->device != e.device) return fail(kErrInvalid, "weight was registered on device %d, current is %d",
                                            e.device, d->device);
-    const int bn = gemm_plan(m, n, k, d->sms, variant).bn;
-    auto mit = e.maps.find(bn);
+    const GemmPlan plan = gemm_plan(m, n, k, d->sms, variant);
+    const int box_rows = gemm_plan_box_rows(plan, false);
+    auto mit = e.maps.find(box_rows);
     if (mit == e.maps.end()) {
       CUtensorMap fresh;
-      if (int rc = gemm_encode_b_map(e.w, e.ldw, e.n, e.k, bn, &fresh)) return rc;
-      mit = e.maps.emplace(bn, fresh).first;
+      if (int rc = gemm_encode_b_map(e.w, e.ldw, e.n, e.k, box_rows, &fresh)) return rc;
+      mit = e.maps.emplace(box_rows, fresh).first;
     }
     map = mit->second;
     map_ptr = &map;
-    variant = bn;
+    variant = gemm_plan_variant(plan);  // the launch takes the same plan the map was encoded for
   }
   return gemm_common(x, ldx, m, k, w, ldw, n, map_ptr, bias, bias_dtype, out, ldo, out_dtype, workspace,
                      workspace_bytes, variant, stream);

@@ -65,10 +65,11 @@ struct GemmArgs {
   KernelCtl ctl;
 };
 
-template <int BN, int STAGES>
+// BROWS: rows of the B tile this CTA holds per stage (BN, or BN/2 for one CTA of a pair).
+template <int BN, int STAGES, int BROWS = BN>
 struct GemmLayout {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
-  static constexpr int kBBytes = BN * kGemmBK * 2;
+  static constexpr int kBBytes = BROWS * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
   // Epilogue staging: per epilogue warp one 32-row x 128-byte tile (128-byte swizzle) for the TMA stores.
@@ -217,15 +218,33 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& m_
   }
 }
 
-template <int BN, int STAGES, int MODE>
+// PAIR: the CTA is one of a cluster of two that share a 256 x BN tile on both SMs' tensor cores (tcgen05
+// cta_group::2). Each CTA loads its own 128 rows of x and its half of the BN weight rows; the leader (rank 0) issues
+// the MMAs, whose commits arrive on both CTAs' barriers; each CTA's epilogue drains its own 128 accumulator rows.
+// Per SM that is 16 KB + BN/2 x 128 B of operands per K block instead of 16 KB + BN x 128 B.
+template <int BN, int STAGES, int MODE, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                              const __grid_constant__ CUtensorMap tm_out, const GemmArgs args) {
-  using L = GemmLayout<BN, STAGES>;
+  using L = GemmLayout<BN, STAGES, PAIR ? BN / 2 : BN>;
   constexpr bool GEGLU = MODE == kModeGeglu;
+  static_assert(!PAIR || (BN % 32 == 0 && BN >= 64), "a pair splits the weight rows of a tile in two 16-row multiples");
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // CTA rank in the pair (0 = leader)
+  constexpr int kTileM = PAIR ? 2 * kGemmBM : kGemmBM;  // output rows per tile
+  // Stage `stage`'s full barrier as the TMA completion target: the leader's, for both CTAs of a pair.
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* full = bars;
+  auto tma2 = [&](const CUtensorMap* map, int stage, uint8_t* dst, int x, int y) {
+    if constexpr (PAIR)
+      tma_load_2d_pair(map, cluster_smem_addr(&full[stage], 0), dst, x, y);
+    else
+      tma_load_2d(map, &full[stage], dst, x, y);
+  };
   // A tile of K block kb for the output rows from m0: a 2-D box of x, or in the convolution form the input patch
   // of tap kb / cblocks (kh, kw) and channel block kb % cblocks, shifted by (kh - 1, kw - 1).
-  auto load_x = [&](uint64_t* bar, uint8_t* dst, int kb, int m0) {
+  auto load_x = [&](int stage, uint8_t* dst, int kb, int m0) {
     if constexpr (MODE == kModeConv3x3) {
       const int tap = kb / args.cv_cblocks;
       const int cb = kb - tap * args.cv_cblocks;
@@ -233,29 +252,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int kw = tap - 3 * kh;
       const int img = m0 / args.cv_hw;
       const int h0 = (m0 - img * args.cv_hw) / args.cv_w;
-      tma_load_4d(&tm_x, bar, dst, cb * kGemmBK, kw - 1, h0 + kh - 1, img);
+      if constexpr (PAIR)
+        tma_load_4d_pair(&tm_x, cluster_smem_addr(&full[stage], 0), dst, cb * kGemmBK, kw - 1, h0 + kh - 1, img);
+      else
+        tma_load_4d(&tm_x, &full[stage], dst, cb * kGemmBK, kw - 1, h0 + kh - 1, img);
     } else {
-      tma_load_2d(&tm_x, bar, dst, kb * kGemmBK, m0);
+      tma2(&tm_x, stage, dst, kb * kGemmBK, m0);
     }
   };
   // Output columns per tile: BN, or BN/2 gated columns in the GEGLU form (a then gate rows of W in the B tile).
   constexpr int kOutCols = GEGLU ? BN / 2 : BN;
   static_assert(!GEGLU || (BN % 64 == 0), "GEGLU tiles hold two halves of a multiple of 32 columns");
-  // W tile of stage i for the output-column block nb: one box of BN rows, or BN/2 a-rows then BN/2 gate-rows.
-  auto load_w = [&](uint64_t* bar, uint8_t* dst, int kb, int nb) {
-    if constexpr (GEGLU) {
-      tma_load_2d(&tm_w, bar, dst, kb * kGemmBK, nb * kOutCols);
-      tma_load_2d(&tm_w, bar, dst + kOutCols * 128, kb * kGemmBK, args.N + nb * kOutCols);
+  // W tile of stage i for the output-column block nb: one box of BN rows, or BN/2 a-rows then BN/2 gate-rows. In a
+  // pair each CTA holds one half: rows [nb*BN + rank*BN/2, +BN/2), or in the GEGLU form the a-rows (leader) or the
+  // gate rows (second CTA).
+  auto load_w = [&](int stage, uint8_t* dst, int kb, int nb) {
+    if constexpr (PAIR) {
+      const int row0 = GEGLU ? (rank == 0 ? nb * kOutCols : args.N + nb * kOutCols) : nb * BN + int(rank) * (BN / 2);
+      tma2(&tm_w, stage, dst, kb * kGemmBK, row0);
+    } else if constexpr (GEGLU) {
+      tma2(&tm_w, stage, dst, kb * kGemmBK, nb * kOutCols);
+      tma2(&tm_w, stage, dst + kOutCols * 128, kb * kGemmBK, args.N + nb * kOutCols);
     } else {
-      tma_load_2d(&tm_w, bar, dst, kb * kGemmBK, nb * BN);
+      tma2(&tm_w, stage, dst, kb * kGemmBK, nb * BN);
     }
   };
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * L::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
-  uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* acc_full = bars + 2 * STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -275,7 +298,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kGemmEpiWarps);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[a], PAIR ? 2 * kGemmEpiWarps : kGemmEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     mbar_init(bias_full, kGemmEpiThreads);  // one arrival per epilogue thread
@@ -288,17 +311,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tm_w);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, L::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, L::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, L::kTmemCols);
+      tmem_relinquish();
+    }
     tc_fence_before();
   }
-  __syncthreads();
+  // A pair's barriers must be initialised in both CTAs before either CTA's copies or commits reach them.
+  if constexpr (PAIR)
+    cluster_sync();
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Let the next kernel on the stream start its prologue on idle SMs; it waits for this grid before reading.
   pdl_launch_dependents();
 
   const int num_units = args.num_tiles * args.splits;
+  // Work units go round the persistent grid; a pair (two consecutive CTAs of a cluster) takes each unit together.
+  const int unit0 = PAIR ? int(blockIdx.x) / 2 : int(blockIdx.x);
+  const int unit_stride = PAIR ? int(gridDim.x) / 2 : int(gridDim.x);
+  // Bytes a stage's full barrier (the leader's, in a pair) expects: both CTAs' tiles in a pair.
+  constexpr uint32_t kFullBytes = PAIR ? 2u * L::kStageBytes : uint32_t(L::kStageBytes);
   const int num_kb = args.num_kb;
 
   if (warp == 0) {
@@ -311,37 +348,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // The weight never depends on the previous kernel on the stream: the first stages' W tiles are requested
       // before waiting on it (programmatic dependent launch), so their fetch overlaps that kernel's tail.
       int pre = 0;
-      if (int(blockIdx.x) < num_units) {
+      if (unit0 < num_units) {
         int mb, nb;
-        tile_coords(args, int(blockIdx.x) / args.splits, mb, nb);
-        const int kb0 = (int(blockIdx.x) % args.splits) * args.kb_per_split;
+        tile_coords(args, unit0 / args.splits, mb, nb);
+        const int kb0 = (unit0 % args.splits) * args.kb_per_split;
         pre = min(STAGES, min(num_kb, kb0 + args.kb_per_split) - kb0);
         for (int i = 0; i < pre; ++i) {
-          mbar_arrive_expect_tx(&full[i], L::kStageBytes);
-          load_w(&full[i], sB + i * L::kBBytes, kb0 + i, nb);
+          if (rank == 0) mbar_arrive_expect_tx(&full[i], kFullBytes);
+          load_w(i, sB + i * L::kBBytes, kb0 + i, nb);
         }
       }
       pdl_wait();  // x may be the previous kernel's output
-      for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+      for (int unit = unit0; ok && unit < num_units; unit += unit_stride) {
         const int tile = unit / args.splits;
         int mb, nb;
         tile_coords(args, tile, mb, nb);
-        const int m0 = mb * kGemmBM;
+        const int m0 = mb * kTileM + int(rank) * kGemmBM;
         const int kb_begin = (unit % args.splits) * args.kb_per_split;
         const int kb_end = min(num_kb, kb_begin + args.kb_per_split);
         for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (pre > 0) {
             // stage already armed and its W tile in flight (first stages of the first unit)
-            load_x(&full[stage], sA + stage * L::kABytes, kb, m0);
+            load_x(stage, sA + stage * L::kABytes, kb, m0);
             --pre;
           } else {
             if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutProducer)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-            load_x(&full[stage], sA + stage * L::kABytes, kb, m0);
-            load_w(&full[stage], sB + stage * L::kBBytes, kb, nb);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], kFullBytes);
+            load_x(stage, sA + stage * L::kABytes, kb, m0);
+            load_w(stage, sB + stage * L::kBBytes, kb, nb);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -350,8 +387,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
-      if (!ok) {
-        // Abort: let the (at most STAGES) loads still in flight land before the CTA's shared memory goes away.
+      if (PAIR && ok) {
+        // Wait until the leader's MMAs have released every stage: their commits arrive on this CTA's barriers, which
+        // must outlive them.
+        for (int i = 0; i < STAGES; ++i) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutProducer)) break;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && rank == 0) {
+        // Abort: let the (at most STAGES) loads still in flight land before the CTA's shared memory goes away (in a
+        // pair the leader's full barriers count both CTAs' loads).
         int s = stage;
         uint32_t ph = phase;
         for (int i = 0; i < min(issued, STAGES); ++i) {
@@ -368,58 +417,83 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     // The whole warp runs the loop (operands stay warp-uniform, which keeps tcgen05.mma issue at the tensor core's
-    // pace); one elected lane issues the MMAs and their commits.
-    constexpr uint32_t kIdesc = idesc_bf16_f32(kGemmBM, BN, false);
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    if (args.ctl.debug & 1u) {
-      // Test hook: wait on a barrier nothing arrives on, so the bounded wait expires and the abort path runs.
-      if (!mbar_wait_bounded_warp(drain, 0, abort_flag, args.ctl, kStatusForced)) ok = false;
-    }
-    int local = 0;
-    for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait_bounded_warp(&acc_empty[acc], acc_phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutMma)) {
-        ok = false;
-        break;
+    // pace); one elected lane issues the MMAs and their commits. In a pair only the leader issues: its MMAs read
+    // both CTAs' stages and write both CTAs' accumulators, and its commits arrive on both CTAs' barriers.
+    constexpr uint32_t kIdesc = idesc_bf16_f32(kTileM, BN, false);
+    constexpr uint16_t kBoth = 3;  // commit multicast mask: both CTAs of the pair
+    auto mma = [&](uint32_t d, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+      if constexpr (PAIR)
+        umma_f16_ss_pair(d, a_desc, b_desc, kIdesc, accumulate);
+      else
+        umma_f16_ss(d, a_desc, b_desc, kIdesc, accumulate);
+    };
+    auto commit = [&](uint64_t* bar, uint16_t mask) {
+      if constexpr (PAIR)
+        umma_commit_pair(bar, mask);
+      else
+        umma_commit(bar);
+    };
+    if (!PAIR || rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      if (args.ctl.debug & 1u) {
+        // Test hook: wait on a barrier nothing arrives on, so the bounded wait expires and the abort path runs.
+        if (!mbar_wait_bounded_warp(drain, 0, abort_flag, args.ctl, kStatusForced)) ok = false;
       }
-      tc_fence_after();
-      const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-      const int kb_begin = (unit % args.splits) * args.kb_per_split;
-      const int kb_end = min(num_kb, kb_begin + args.kb_per_split);
-      for (int kb = kb_begin; kb < kb_end; ++kb) {
-        if (!mbar_wait_bounded_warp(&full[stage], phase, abort_flag, args.ctl, kStatusTimeoutMma)) {
+      int local = 0;
+      for (int unit = unit0; ok && unit < num_units; unit += unit_stride, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded_warp(&acc_empty[acc], acc_phase ^ 1u, abort_flag, args.ctl, kStatusTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t a_desc = smem_desc_kmajor_sw128(smem_u32(sA + stage * L::kABytes));
-        const uint64_t b_desc = smem_desc_kmajor_sw128(smem_u32(sB + stage * L::kBBytes));
-        if (elect_one()) {
-#pragma unroll
-          for (int k = 0; k < kGemmBK / 16; ++k) {
-            // +32 bytes per K step of 16 bf16 inside the swizzle atom (descriptor address field is >> 4).
-            umma_f16_ss(d_tmem, a_desc + 2u * k, b_desc + 2u * k, kIdesc, (kb > kb_begin || k > 0) ? 1u : 0u);
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        const int kb_begin = (unit % args.splits) * args.kb_per_split;
+        const int kb_end = min(num_kb, kb_begin + args.kb_per_split);
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
+          if (!mbar_wait_bounded_warp(&full[stage], phase, abort_flag, args.ctl, kStatusTimeoutMma)) {
+            ok = false;
+            break;
           }
-          umma_commit(&empty[stage]);  // frees the smem stage once these MMAs have read it
+          tc_fence_after();
+          const uint64_t a_desc = smem_desc_kmajor_sw128(smem_u32(sA + stage * L::kABytes));
+          const uint64_t b_desc = smem_desc_kmajor_sw128(smem_u32(sB + stage * L::kBBytes));
+          if (elect_one()) {
+#pragma unroll
+            for (int k = 0; k < kGemmBK / 16; ++k) {
+              // +32 bytes per K step of 16 bf16 inside the swizzle atom (descriptor address field is >> 4).
+              mma(d_tmem, a_desc + 2u * k, b_desc + 2u * k, (kb > kb_begin || k > 0) ? 1u : 0u);
+            }
+            commit(&empty[stage], kBoth);  // frees the smem stage (in both CTAs) once these MMAs have read it
+          }
+          __syncwarp();
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
+        if (!ok) break;
+        if (elect_one()) commit(&acc_full[acc], kBoth);  // accumulator complete
         __syncwarp();
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
+      }
+      if (PAIR && ok) {
+        // Wait until both CTAs' epilogues have released the last two accumulators: the second CTA's releases are
+        // arrivals on this CTA's barriers, which must outlive them.
+        for (int i = 0; i < 2; ++i, ++local) {
+          if (!mbar_wait_bounded_warp(&acc_empty[local & 1], ((local >> 1) & 1) ^ 1u, abort_flag, args.ctl,
+                                      kStatusTimeoutMma))
+            break;
         }
       }
-      if (!ok) break;
-      if (elect_one()) umma_commit(&acc_full[acc]);  // accumulator complete
-      __syncwarp();
-    }
-    if (!ok) {
-      // Abort: wait until every MMA this warp issued has finished before TMEM is released.
-      if (elect_one()) umma_commit(drain);
-      __syncwarp();
-      mbar_wait_drain(drain, 0u, args.ctl);
+      if (!ok) {
+        // Abort: wait until every MMA this warp issued has finished before TMEM is released.
+        if (elect_one()) commit(drain, 1);
+        __syncwarp();
+        mbar_wait_drain(drain, 0u, args.ctl);
+      }
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..9)
@@ -440,7 +514,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool table_bias = args.bias != nullptr && args.bias_img_stride == 0;
     float* bias_tab = reinterpret_cast<float*>(smem + L::kBiasOffset);
     pdl_wait();  // the previous kernel may still read (or write) the output / bias
-    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++local) {
+    for (int unit = unit0; unit < num_units; unit += unit_stride, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (args.bias != nullptr && warp == 2) {
@@ -459,7 +533,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int split = unit % splits;
       int mb, nb;
       tile_coords(args, tile, mb, nb);
-      const int m0 = mb * kGemmBM;
+      const int m0 = mb * kTileM + int(rank) * kGemmBM;  // this CTA's 128 rows of the tile
       const int n0 = nb * kOutCols;
       if (table_bias) {
         // This tile's bias table: each epilogue thread fetches up to two entries (requested before any wait),
@@ -625,16 +699,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(cluster_smem_addr(&acc_empty[acc], 0));  // the leader's MMA waits on it
+        else
+          mbar_arrive(&acc_empty[acc]);
+      }
       if (table_bias) mbar_arrive(bias_free);
     }
     if (args.tma_store && lane == 0) bulk_wait_read<0>();  // staging must not be released while being read
   }
 
-  __syncthreads();
+  // Nothing of either CTA of a pair may be freed while the other can still reach it.
+  if constexpr (PAIR)
+    cluster_sync();
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, L::kTmemCols);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, L::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, L::kTmemCols);
   }
 }
 
@@ -643,29 +729,52 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ---------------------------------------------------------------------------------------------------------------
 namespace {
 
-template <int BN, int STAGES, int MODE = kModePlain>
+// Launch one instantiation as a persistent grid over `units` work units: one CTA per SM, or for a pair variant one
+// two-CTA cluster per SM pair (as many clusters as can be resident at once, from the occupancy query).
+template <int BN, int STAGES, int MODE = kModePlain, bool PAIR = false>
 int launch_variant(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mo, const GemmArgs& args,
-                   int grid, cudaStream_t st, int device) {
-  using L = GemmLayout<BN, STAGES>;
+                   int64_t units, int sms, cudaStream_t st, int device) {
+  using L = GemmLayout<BN, STAGES, PAIR ? BN / 2 : BN>;
   static bool configured[64] = {false};
-  auto kern = gemm_bf16_tcgen05_kernel<BN, STAGES, MODE>;
+  static int resident_clusters[64] = {0};
+  auto kern = gemm_bf16_tcgen05_kernel<BN, STAGES, MODE, PAIR>;
   if (device < 0 || device >= 64) return fail(kErrInvalid, "device ordinal %d out of range", device);
   if (!configured[device]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm smem)");
+    if (PAIR) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+      if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm cluster)");
+    }
     configured[device] = true;
   }
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = L::kSmemBytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = PAIR ? 2 : 1;
+  int grid = int(std::min<int64_t>(units, sms));
+  if (PAIR) {
+    if (resident_clusters[device] == 0) {
+      cfg.gridDim = dim3(unsigned(2 * (sms / 2)));
+      int n = 0;
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) return check_cuda(e, "cudaOccupancyMaxActiveClusters(gemm)");
+      if (n < 1) return fail(kErrUnsupported, "no two-CTA cluster of the GEMM fits on this device");
+      resident_clusters[device] = n;
+    }
+    grid = 2 * int(std::min<int64_t>(units, resident_clusters[device]));
+  }
+  cfg.gridDim = dim3(unsigned(grid));
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, mx, mw, mo, args), "gemm kernel launch");
 }
 
@@ -727,11 +836,39 @@ double plan_cost(int64_t M, int64_t N, int64_t kb, int bn, int splits, int sms) 
 }
 }  // namespace
 
-GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool geglu) {
+namespace {
+// Modelled time of a paired plan: tiles of 256 x BN rows x columns, one per two-CTA cluster (about sms / 2
+// resident). Per SM the tensor core does the same work per K block as for a one-CTA BN tile while only half of B
+// arrives in its shared memory; measured on B200 that makes the main loop about 8% faster for BN = 256 (less for
+// narrower tiles, which never won), against about 1 us more per launch (cluster launch, the pair's hand-offs and
+// teardown), so pairs pay only for long-running wide tiles.
+double plan_cost_pair(int64_t M, int64_t N, int64_t kb, int bn, int sms) {
+  const int64_t tiles = ((M + 2 * kGemmBM - 1) / (2 * kGemmBM)) * ((N + bn - 1) / bn);
+  const int64_t clusters = std::max(1, sms / 2);
+  const int64_t waves = (tiles + clusters - 1) / clusters;
+  const double mma = 2.0 * bn;
+  const double load = (kGemmBM + bn) * 128.0 / 64.0;
+  return double(waves) * (0.92 * double(kb) * std::max(mma, load) + 1500.0 + 8.0 * bn) + 2000.0;
+}
+
+bool pair_tile(int bn) { return bn == 128 || bn == 192 || bn == 256; }
+
+}  // namespace
+
+bool gemm_variant_known(int variant, bool geglu) {
+  const bool pair = variant >= kGemmPairVariant;
+  const int bn = pair ? variant - kGemmPairVariant : variant;
+  bool known = false;
+  for (int c : kTileChoices) known |= (c == bn);
+  return known && (!pair || pair_tile(bn)) && (!geglu || bn % 64 == 0);
+}
+
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool geglu, bool auto_pair) {
   // N counts accumulator columns: for the GEGLU form the 2 x inner projection columns, and only tiles with an even
-  // split into a and gate halves of 32-column multiples are candidates.
+  // split into a and gate halves of 32-column multiples are candidates. `variant` (when not 0) forces one tile:
+  // BN, or kGemmPairVariant + BN for the paired form.
   const int64_t kb = (K + kGemmBK - 1) / kGemmBK;
-  GemmPlan best{128, 1, int(kb), 0};
+  GemmPlan best{128, 1, int(kb), 0, false};
   double best_cost = 1e300;
   for (int bn : kTileChoices) {
     if (variant && bn != variant) continue;
@@ -740,7 +877,8 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool g
     // Split K only when the tiles leave most SMs idle and each split keeps >= 4 K blocks (never for GEGLU, whose
     // gating needs the finished sums).
     int max_split = 1;
-    if (!geglu && tiles * 2 <= sms && tiles * 4 <= int64_t(kSplitCounterBytes) && kb >= 8) max_split = int(std::min<int64_t>(std::min<int64_t>(sms / tiles, kb / 4), 16));
+    if (!geglu && tiles * 2 <= sms && tiles * 4 <= int64_t(kSplitCounterBytes) && kb >= 8)
+      max_split = int(std::min<int64_t>(std::min<int64_t>(sms / tiles, kb / 4), 16));
     for (int sp = 1; sp <= max_split; ++sp) {
       const int kps = int((kb + sp - 1) / sp);
       const int eff = int((kb + kps - 1) / kps);  // splits actually needed with kps blocks each
@@ -755,11 +893,23 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool g
       }
     }
   }
+  // Paired tiles (never with split K): automatically only 256-column tiles over at least 20 K blocks outside the
+  // GEGLU form (shorter tiles are bound by their epilogue, which the pair does not speed up), when the output has
+  // at least two 128-row blocks; any pair tile when forced.
+  for (int bn : kTileChoices) {
+    if (!pair_tile(bn) || (geglu && bn % 64 != 0) || M <= kGemmBM) continue;
+    if (variant ? variant != kGemmPairVariant + bn : (!auto_pair || bn != 256 || geglu || kb < 20)) continue;
+    const double cost = plan_cost_pair(M, N, kb, bn, sms);
+    if (variant || cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = GemmPlan{bn, 1, int(kb), 0, true};
+    }
+  }
   return best;
 }
 
-int gemm_encode_b_map(const void* w, int64_t ldw, int64_t N, int64_t K, int bn, CUtensorMap* out) {
-  return encode_kmajor_map(w, N, K, ldw, bn, out);
+int gemm_encode_b_map(const void* w, int64_t ldw, int64_t N, int64_t K, int box_rows, CUtensorMap* out) {
+  return encode_kmajor_map(w, N, K, ldw, box_rows, out);
 }
 
 int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
@@ -770,12 +920,8 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   if (p.M > INT32_MAX / 2 || p.N > INT32_MAX / 2 || p.K > INT32_MAX / 2)
     return fail(kErrInvalid, "GEMM dimension too large");
   const bool geglu = p.geglu != 0;
-  if (p.variant) {
-    bool known = false;
-    for (int c : kTileChoices) known |= (c == p.variant) && (!geglu || c % 64 == 0);
-    if (!known)
-      return fail(kErrUnsupported, "no GEMM%s variant with an N tile of %d", geglu ? " (GEGLU)" : "", p.variant);
-  }
+  if (p.variant && !gemm_variant_known(p.variant, geglu))
+    return fail(kErrUnsupported, "no GEMM%s variant %d", geglu ? " (GEGLU)" : "", p.variant);
   if (geglu && p.w_map_cache != nullptr) return fail(kErrInvalid, "the GEGLU form encodes its own weight map");
   GemmPlan plan = gemm_plan(p.M, geglu ? 2 * p.N : p.N, p.K, dev->sms, p.variant, geglu);
   const int bn = plan.bn;
@@ -789,8 +935,9 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   CUtensorMap mx, mw;
   if (int rc = encode_kmajor_map(p.x, p.M, p.K, p.ldx, kGemmBM, &mx)) return rc;
   if (p.w_map_cache != nullptr) {
-    mw = *p.w_map_cache;
-  } else if (int rc = encode_kmajor_map(p.w, geglu ? 2 * p.N : p.N, p.K, p.ldw, geglu ? bn / 2 : bn, &mw)) {
+    mw = *p.w_map_cache;  // encoded with gemm_plan_box_rows(plan) rows per box
+  } else if (int rc = encode_kmajor_map(p.w, geglu ? 2 * p.N : p.N, p.K, p.ldw, gemm_plan_box_rows(plan, geglu),
+                                        &mw)) {
     return rc;
   }
 
@@ -807,7 +954,8 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.M = int(p.M);
   a.N = int(p.N);
   a.K = int(p.K);
-  a.num_m_blk = int((p.M + kGemmBM - 1) / kGemmBM);
+  const int tile_m = plan.pair ? 2 * kGemmBM : kGemmBM;
+  a.num_m_blk = int((p.M + tile_m - 1) / tile_m);
   const int num_n = int((p.N + out_cols - 1) / out_cols);
   a.num_n_blk = num_n;
   // Raster: keep the larger operand's tiles in L2 while the smaller one streams past them.
@@ -832,24 +980,42 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.ctl.status = dev->status;
   a.ctl.timeout_ns = wait_timeout_ns();
   a.ctl.debug = p.debug;
-  const int grid = int(std::min<int64_t>(tiles * plan.splits, dev->sms));
+  const int64_t units = tiles * plan.splits;
+  const int sms = dev->sms;
+  const int d = dev->device;
 
+  if (plan.pair) {
+    if (geglu) {
+      switch (bn) {
+        case 128: return launch_variant<128, 8, kModeGeglu, true>(mx, mw, mo, a, units, sms, stream, d);
+        case 192: return launch_variant<192, 6, kModeGeglu, true>(mx, mw, mo, a, units, sms, stream, d);
+        case 256: return launch_variant<256, 6, kModeGeglu, true>(mx, mw, mo, a, units, sms, stream, d);
+      }
+    } else {
+      switch (bn) {
+        case 128: return launch_variant<128, 8, kModePlain, true>(mx, mw, mo, a, units, sms, stream, d);
+        case 192: return launch_variant<192, 6, kModePlain, true>(mx, mw, mo, a, units, sms, stream, d);
+        case 256: return launch_variant<256, 6, kModePlain, true>(mx, mw, mo, a, units, sms, stream, d);
+      }
+    }
+    return fail(kErrUnsupported, "no paired GEMM variant with an N tile of %d", bn);
+  }
   if (geglu) {
     switch (bn) {
-      case 64: return launch_variant<64, 8, kModeGeglu>(mx, mw, mo, a, grid, stream, dev->device);
-      case 128: return launch_variant<128, 6, kModeGeglu>(mx, mw, mo, a, grid, stream, dev->device);
-      case 192: return launch_variant<192, 4, kModeGeglu>(mx, mw, mo, a, grid, stream, dev->device);
-      case 256: return launch_variant<256, 4, kModeGeglu>(mx, mw, mo, a, grid, stream, dev->device);
+      case 64: return launch_variant<64, 8, kModeGeglu>(mx, mw, mo, a, units, sms, stream, d);
+      case 128: return launch_variant<128, 6, kModeGeglu>(mx, mw, mo, a, units, sms, stream, d);
+      case 192: return launch_variant<192, 4, kModeGeglu>(mx, mw, mo, a, units, sms, stream, d);
+      case 256: return launch_variant<256, 4, kModeGeglu>(mx, mw, mo, a, units, sms, stream, d);
     }
     return fail(kErrUnsupported, "no GEGLU GEMM variant with an N tile of %d", bn);
   }
   switch (bn) {
-    case 64: return launch_variant<64, 8>(mx, mw, mo, a, grid, stream, dev->device);
-    case 96: return launch_variant<96, 6>(mx, mw, mo, a, grid, stream, dev->device);
-    case 128: return launch_variant<128, 6>(mx, mw, mo, a, grid, stream, dev->device);
-    case 160: return launch_variant<160, 5>(mx, mw, mo, a, grid, stream, dev->device);
-    case 192: return launch_variant<192, 4>(mx, mw, mo, a, grid, stream, dev->device);
-    case 256: return launch_variant<256, 4>(mx, mw, mo, a, grid, stream, dev->device);
+    case 64: return launch_variant<64, 8>(mx, mw, mo, a, units, sms, stream, d);
+    case 96: return launch_variant<96, 6>(mx, mw, mo, a, units, sms, stream, d);
+    case 128: return launch_variant<128, 6>(mx, mw, mo, a, units, sms, stream, d);
+    case 160: return launch_variant<160, 5>(mx, mw, mo, a, units, sms, stream, d);
+    case 192: return launch_variant<192, 4>(mx, mw, mo, a, units, sms, stream, d);
+    case 256: return launch_variant<256, 4>(mx, mw, mo, a, units, sms, stream, d);
   }
   return fail(kErrUnsupported, "no GEMM variant with an N tile of %d", bn);
 }
@@ -881,13 +1047,12 @@ int conv3x3_launch(const ConvProblem& p, cudaStream_t stream) {
     return fail(kErrInvalid, "conv3x3 input and weight must be 16-byte aligned");
   if (p.ldo < p.cout) return fail(kErrInvalid, "conv3x3 output row stride below the channel count");
   if (p.residual != nullptr && p.ldr < p.cout) return fail(kErrInvalid, "conv3x3 residual row stride too small");
-  if (p.variant) {
-    bool known = false;
-    for (int c : kTileChoices) known |= (c == p.variant);
-    if (!known) return fail(kErrUnsupported, "no conv3x3 variant with an output-channel tile of %d", p.variant);
-  }
-  GemmPlan plan = gemm_plan(M, p.cout, K, dev->sms, p.variant);
+  if (p.variant && !gemm_variant_known(p.variant, false))
+    return fail(kErrUnsupported, "no conv3x3 variant %d", p.variant);
+  // Pairs only when forced: on the SD1.5 convolutions they measured level with or slower than one-CTA tiles.
+  GemmPlan plan = gemm_plan(M, p.cout, K, dev->sms, p.variant, false, false);
   const int bn = plan.bn;
+  const int tile_m = plan.pair ? 2 * kGemmBM : kGemmBM;
   if (plan.splits > 1 && (p.ws_split == nullptr || p.ws_split_bytes < plan.split_ws_bytes ||
                           (reinterpret_cast<uintptr_t>(p.ws_split) & 255) != 0)) {
     plan.splits = 1;  // no room for partials: one CTA per tile over all of K
@@ -907,7 +1072,7 @@ int conv3x3_launch(const ConvProblem& p, cudaStream_t stream) {
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(kErrInvalid, "cuTensorMapEncodeTiled failed (%d) for the conv input", int(r));
   }
-  if (int rc = encode_kmajor_map(p.wt, p.cout, K, K, bn, &mw)) return rc;
+  if (int rc = encode_kmajor_map(p.wt, p.cout, K, K, plan.pair ? bn / 2 : bn, &mw)) return rc;
   memset(&mo, 0, sizeof(mo));
   const int esz = p.out_f32 ? 4 : 2;
   bool tma_store = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && (p.ldo * esz) % 16 == 0;
@@ -919,7 +1084,7 @@ int conv3x3_launch(const ConvProblem& p, cudaStream_t stream) {
   a.M = int(M);
   a.N = int(p.cout);
   a.K = int(K);
-  a.num_m_blk = int((M + kGemmBM - 1) / kGemmBM);
+  a.num_m_blk = int((M + tile_m - 1) / tile_m);
   a.num_n_blk = int((p.cout + bn - 1) / bn);
   a.n_fastest = 1;  // the input patch stays in L2 while the output-channel tiles of a pixel tile go by
   a.num_tiles = a.num_m_blk * a.num_n_blk;
@@ -946,21 +1111,31 @@ int conv3x3_launch(const ConvProblem& p, cudaStream_t stream) {
   a.ctl.status = dev->status;
   a.ctl.timeout_ns = wait_timeout_ns();
   a.ctl.debug = p.debug;
-  const int grid = int(std::min<int64_t>(int64_t(a.num_tiles) * plan.splits, dev->sms));
+  const int64_t units = int64_t(a.num_tiles) * plan.splits;
+  const int sms = dev->sms;
+  const int d = dev->device;
+  if (plan.pair) {
+    switch (bn) {
+      case 128: return launch_variant<128, 8, kModeConv3x3, true>(mx, mw, mo, a, units, sms, stream, d);
+      case 192: return launch_variant<192, 6, kModeConv3x3, true>(mx, mw, mo, a, units, sms, stream, d);
+      case 256: return launch_variant<256, 6, kModeConv3x3, true>(mx, mw, mo, a, units, sms, stream, d);
+    }
+    return fail(kErrUnsupported, "no paired conv3x3 variant with an output-channel tile of %d", bn);
+  }
   switch (bn) {
-    case 64: return launch_variant<64, 8, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
-    case 96: return launch_variant<96, 6, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
-    case 128: return launch_variant<128, 6, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
-    case 160: return launch_variant<160, 5, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
-    case 192: return launch_variant<192, 4, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
-    case 256: return launch_variant<256, 4, kModeConv3x3>(mx, mw, mo, a, grid, stream, dev->device);
+    case 64: return launch_variant<64, 8, kModeConv3x3>(mx, mw, mo, a, units, sms, stream, d);
+    case 96: return launch_variant<96, 6, kModeConv3x3>(mx, mw, mo, a, units, sms, stream, d);
+    case 128: return launch_variant<128, 6, kModeConv3x3>(mx, mw, mo, a, units, sms, stream, d);
+    case 160: return launch_variant<160, 5, kModeConv3x3>(mx, mw, mo, a, units, sms, stream, d);
+    case 192: return launch_variant<192, 4, kModeConv3x3>(mx, mw, mo, a, units, sms, stream, d);
+    case 256: return launch_variant<256, 4, kModeConv3x3>(mx, mw, mo, a, units, sms, stream, d);
   }
   return fail(kErrUnsupported, "no conv3x3 variant with an output-channel tile of %d", bn);
 }
 
 size_t conv3x3_workspace_bytes(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant, int sms) {
   if (n <= 0 || h <= 0 || w <= 0 || cin <= 0 || cout <= 0 || sms <= 0) return 0;
-  return gemm_plan(n * h * w, cout, 9 * cin, sms, variant).split_ws_bytes;
+  return gemm_plan(n * h * w, cout, 9 * cin, sms, variant, false, false).split_ws_bytes;
 }
 
 // ---------------------------------------------------------------------------------------------------------------

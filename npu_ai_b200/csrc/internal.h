@@ -68,9 +68,17 @@ struct GemmPlan {
   int splits;
   int kb_per_split;
   size_t split_ws_bytes;  // bytes of split-K workspace the plan needs (0 when splits == 1)
+  bool pair;              // 256-row tiles on a two-CTA cluster (tcgen05 cta_group::2)
 };
-GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool geglu = false);
-int gemm_encode_b_map(const void* w, int64_t ldw, int64_t N, int64_t K, int bn, CUtensorMap* out);
+// Tile variants: BN (64 ... 256) for one CTA per tile, kGemmPairVariant + BN (128, 192, 256) for a CTA pair.
+constexpr int kGemmPairVariant = 1000;
+bool gemm_variant_known(int variant, bool geglu);
+// auto_pair: whether the automatic choice (variant 0) may pick a pair tile.
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool geglu = false, bool auto_pair = true);
+inline int gemm_plan_variant(const GemmPlan& p) { return p.pair ? kGemmPairVariant + p.bn : p.bn; }
+// Weight rows per TMA box: BN, or BN/2 for the GEGLU form (a and gate halves) and for one CTA of a pair.
+inline int gemm_plan_box_rows(const GemmPlan& p, bool geglu) { return (p.pair || geglu) ? p.bn / 2 : p.bn; }
+int gemm_encode_b_map(const void* w, int64_t ldw, int64_t N, int64_t K, int box_rows, CUtensorMap* out);
 // Bytes of workspace the GEMM entry points use for a problem (split-K counters + partials, repack buffers).
 size_t gemm_workspace_bytes(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,
                             int variant, int sms, int geglu = 0);

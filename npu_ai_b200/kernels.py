@@ -43,7 +43,8 @@ def register_weight(w_nk: torch.Tensor) -> int:
 
 
 def gemm_plan(M: int, N: int, K: int, variant: int = 0, device: torch.device | int | None = None) -> tuple[int, int]:
-    """(N tile, split-K factor) the library picks for an M x K x N GEMM on the device."""
+    """(tile variant, split-K factor) the library picks for an M x K x N GEMM on the device. The variant is the N
+    tile (64 ... 256), or 1000 + the N tile for 256-row tiles shared by a two-CTA cluster."""
     bn, sp = ctypes.c_int(0), ctypes.c_int(0)
     with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
         _lib.call("npub200_gemm_plan", int(M), int(N), int(K), int(variant), ctypes.byref(bn), ctypes.byref(sp))

@@ -15,7 +15,7 @@ the NPU runner (its ComfyUI node, its test scripts) run unchanged:
 What changes on B200 (and why):
   * Device: one CUDA device instead of an NPU; tensors live in HBM. Inputs may be CPU (copied over) or CUDA
     tensors; results are CUDA tensors (f32 by default, the reference's output type; `out_dtype=torch.bfloat16`
-    gives the BASELINE's bf16 output).
+    gives bf16 output, the benchmarked configuration's).
   * No padding and no chunking: the kernels take any M, N, K (ragged tails in-kernel) and any sequence length, so
     the NPU alignment (M % 256, K % 64, N % 320) and chunk limits (xdna1_gemm.py:220-229, :274-293) disappear. The
     NPU-only constructor arguments are accepted and recorded but do not change the computation.

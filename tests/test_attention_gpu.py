@@ -1,8 +1,8 @@
 """Fused attention parity on the B200: the tcgen05 flash kernel through the C ABI against the CPU oracle.
 
 Semantics follow the reference's attention test (scripts/11-attn-fused-test.py: seeded q, k ~ 1.5 N(0,1) and
-v ~ N(0,1), SDPA in f32 as the reference, max|err|/max|ref|, padded-stride views) and the BASELINE configs
-(q/k/v ~ N(0,1), scale 1/sqrt(d)), with the north star's tolerance: max-abs <= 2e-2 against SDPA in f32 on
+v ~ N(0,1), SDPA in f32 as the reference, max|err|/max|ref|, padded-stride views) and the benchmarked attention
+blocks (q/k/v ~ N(0,1), scale 1/sqrt(d)), with the stated tolerance: max-abs <= 2e-2 against SDPA in f32 on
 bf16-rounded inputs.
 """
 import functools

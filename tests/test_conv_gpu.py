@@ -45,9 +45,21 @@ def test_conv3x3_shapes(cuda_device, shape):
     _check_bf16(_run(x, wt, b, out_dtype=torch.bfloat16), ref)
 
 
-@pytest.mark.parametrize("variant", [64, 96, 128, 160, 192, 256])
+@pytest.mark.parametrize("variant", [64, 96, 128, 160, 192, 256, 1128, 1192, 1256])
 def test_conv3x3_every_tile(cuda_device, variant):
     x, wt, b = _inputs(2, 16, 16, 320, 640, seed=variant)
+    _check_f32(_run(x, wt, b, variant=variant), conv3x3_ref(x, wt, b))
+
+
+@pytest.mark.parametrize("variant", [1128, 1256])
+def test_conv3x3_pair_tiles_ragged(cuda_device, variant):
+    """256-pixel tiles on a two-CTA cluster where the last tile's second CTA starts past the last image (3 images
+    of 8x8 = 192 pixels) and a per-image bias row plus a residual in the epilogue."""
+    x, wt, b = _inputs(3, 8, 8, 64, 96, seed=variant)
+    g = torch.Generator().manual_seed(variant)
+    b2 = b[None, :] + torch.randn(3, 96, generator=g)
+    res = torch.randn(3, 8, 8, 96, generator=g).to(torch.bfloat16)
+    _check_f32(_run(x, wt, b2, res, variant=variant), conv3x3_ref(x, wt, b2, res))
     _check_f32(_run(x, wt, b, variant=variant), conv3x3_ref(x, wt, b))
 
 

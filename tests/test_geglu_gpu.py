@@ -43,7 +43,7 @@ def test_geglu_shapes(cuda_device, shape):
     _check_bf16(_run(x, w, b, torch.bfloat16), ref)
 
 
-@pytest.mark.parametrize("variant", [64, 128, 192, 256])
+@pytest.mark.parametrize("variant", [64, 128, 192, 256, 1128, 1192, 1256])
 def test_geglu_every_tile(cuda_device, variant):
     """Each accumulator tile (half value, half gate columns), including 192 whose 96 output columns end in a
     remainder chunk, on a shape with ragged M and n."""

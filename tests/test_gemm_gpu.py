@@ -1,7 +1,7 @@
 """GEMM parity on the B200: the tcgen05 kernel through the C ABI against the CPU oracle.
 
 Semantics follow the reference's GEMM test (scripts/05-gemm-test.py: seeded inputs, torch CPU reference on
-bf16-rounded inputs in f32, max|err|/max|ref| and cosine, an unaligned 100x100x100 case) with the north star's
+bf16-rounded inputs in f32, max|err|/max|ref| and cosine, an unaligned 100x100x100 case) with the offload path's
 stated tolerance: max-abs <= 2e-2 and relative L2 <= 5e-3 on the f32 output. bf16 outputs are compared with the
 oracle rounded to bf16: at most 1 bf16 ulp apart (accumulation order can flip a rounding), never more.
 """
@@ -55,7 +55,8 @@ def _run(x, w, b, out_dtype=torch.float32, variant=0):
 
 
 def test_config1_linear_to_q(cuda_device):
-    """x [4096x320] ~N(0,1), W [320x320] ~N(0,0.02^2), b ~N(0,0.01^2), f32 acc, bf16 out."""
+    """SD1.5 to_q at the 64x64 latent: x [4096x320] ~N(0,1), W [320x320] ~N(0,0.02^2), b ~N(0,0.01^2), f32
+    accumulate, bf16 out."""
     x, w, b = _inputs(4096, 320, 320)
     ref = linear_ref(x, w, b)
     _check_f32(_run(x, w, b, torch.float32), ref)
@@ -77,10 +78,14 @@ def test_sd15_bf16_out(cuda_device, MKN):
     _check_bf16(_run(x, w, b, torch.bfloat16), linear_ref(x, w, b))
 
 
-@pytest.mark.parametrize("variant", [64, 96, 128, 160, 192, 256])
+@pytest.mark.parametrize("variant", [64, 96, 128, 160, 192, 256, 1128, 1192, 1256])
 def test_forced_variants(cuda_device, variant):
-    x, w, b = _inputs(1000, 704, 1000, seed=variant)
-    _check_f32(_run(x, w, b, variant=variant), linear_ref(x, w, b))
+    """Every tile variant, 1000 + N tile being 256-row tiles on a two-CTA cluster; M = 1100 leaves the last
+    256-row tile's second CTA with 76 rows, M = 1000 a ragged last row block."""
+    for M in (1000, 1100):
+        x, w, b = _inputs(M, 704, 1000, seed=variant + M)
+        _check_f32(_run(x, w, b, variant=variant), linear_ref(x, w, b))
+        _check_bf16(_run(x, w, b, torch.bfloat16, variant=variant), linear_ref(x, w, b))
 
 
 @pytest.mark.parametrize("MKN", [(1, 8, 8), (1, 320, 320), (3, 16, 17), (129, 72, 200), (255, 1024, 33),
