@@ -132,6 +132,14 @@ int npub200_group_norm(const void* x, int64_t n, int64_t hw, int64_t c, int64_t 
                        const float* beta, float eps, int apply_silu, void* out, float* stats, void* stream);
 int npub200_group_norm_scratch_size(int64_t n, int64_t groups, size_t* bytes_out);
 
+/* LayerNorm over the last dimension of bf16 rows (norm1/norm2/norm3 of every SD1.5 transformer block, which the
+ * reference leaves on the host, docs/02-results.md:411-413): out[r][j] = (x[r][j] - mean_r) * rstd_r * gamma[j] +
+ * beta[j], mean and variance of row r over its cols values in f32, bf16 out. x: [rows][ldx], out: [rows][ldo];
+ * cols, ldx, ldo multiples of 8, cols <= 2048, tensors 16-byte aligned; gamma, beta: [cols] of param_dtype (f32 or
+ * bf16). Deterministic (fixed-order reductions); allocates nothing. */
+int npub200_layer_norm(const void* x, int64_t rows, int64_t cols, int64_t ldx, const void* gamma, const void* beta,
+                       int param_dtype, float eps, void* out, int64_t ldo, void* stream);
+
 /* ----------------------------------------------------------------------------------------------------------
  * GEMM without a workspace, for callers that cannot allocate device memory (a host whose device memory is owned
  * by its own pool manager and may not grow during a request, an FFI binding holding only the pointers it was

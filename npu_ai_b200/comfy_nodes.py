@@ -140,6 +140,8 @@ class B200Runtime:
         # (attn1 out Linear, attn2 out Linear, feed-forward out Linear); pending_res: id(Linear) -> residual.
         self.tblocks: dict[int, tuple] = {}
         self.pending_res: dict[int, torch.Tensor] = {}
+        # LayerNorms of those blocks (norm1/norm2/norm3) on the row-wise LayerNorm kernel: id -> (f32 gamma, beta).
+        self.lnorms: dict[int, tuple] = {}
         self.enabled = False
         self.record_only = False
         self.recorded: set[tuple[int, int, int]] = set()
@@ -171,6 +173,18 @@ class B200Runtime:
                 self.tblocks[id(mod)] = plan
                 self.installed[id(mod)] = (mod, mod.forward)
                 mod.forward = types.MethodType(_gpu_tblock_forward, mod)
+        for mod in diffusion_model.modules():
+            if id(mod) not in self.tblocks:
+                continue
+            for nm in ("norm1", "norm2", "norm3"):
+                ln = getattr(mod, nm, None)
+                if (isinstance(ln, torch.nn.LayerNorm) and ln.elementwise_affine and ln.bias is not None
+                        and len(ln.normalized_shape) == 1 and ln.normalized_shape[0] % 8 == 0
+                        and ln.normalized_shape[0] <= 2048 and id(ln) not in self.installed):
+                    self.lnorms[id(ln)] = (ln.weight.detach().to(self.gemm.device, torch.float32).contiguous(),
+                                           ln.bias.detach().to(self.gemm.device, torch.float32).contiguous())
+                    self.installed[id(ln)] = (ln, ln.forward)
+                    ln.forward = types.MethodType(_gpu_layer_norm_forward, ln)
         if convolutions:
             self._take_over_convs(diffusion_model)
         # GEGLU feed-forward blocks whose projection was taken over: projection + gating in one kernel.
@@ -268,6 +282,7 @@ class B200Runtime:
                 wt.release()
         self.convs.clear()
         self.norms.clear()
+        self.lnorms.clear()
         self.resblocks.clear()
         self.tblocks.clear()
         self.pending_res.clear()
@@ -445,6 +460,19 @@ def _gpu_group_norm_forward(self, x: torch.Tensor) -> torch.Tensor:
     kernels.group_norm(x.permute(0, 2, 3, 1), self.num_groups, entry[0], entry[1], eps=self.eps,
                        out=out.permute(0, 2, 3, 1))
     return out
+
+
+def _gpu_layer_norm_forward(self, x: torch.Tensor) -> torch.Tensor:
+    """LayerNorm.forward (norm1/norm2/norm3 of a taken-over transformer block) on the row-wise LayerNorm kernel for
+    contiguous bf16 CUDA activations; anything else takes the module's own forward."""
+    rt = _RUNTIME
+    entry = rt.lnorms.get(id(self)) if rt is not None else None
+    if (entry is None or not _runtime_on(rt) or not isinstance(x, torch.Tensor) or not x.is_cuda
+            or x.dtype != torch.bfloat16 or not x.is_contiguous() or x.shape[-1] != entry[0].shape[0]):
+        return rt.installed[id(self)][1](x) if rt is not None and id(self) in rt.installed else \
+            torch.nn.LayerNorm.forward(self, x)
+    from . import kernels
+    return kernels.layer_norm(x, entry[0], entry[1], eps=self.eps)
 
 
 def _resblock_plan(mod, rt):

@@ -375,6 +375,14 @@ int npub200_group_norm(const void* x, int64_t n, int64_t hw, int64_t c, int64_t 
                            static_cast<cudaStream_t>(stream));
 }
 
+int npub200_layer_norm(const void* x, int64_t rows, int64_t cols, int64_t ldx, const void* gamma, const void* beta,
+                       int param_dtype, float eps, void* out, int64_t ldo, void* stream) {
+  if (param_dtype != NPUB200_DTYPE_F32 && param_dtype != NPUB200_DTYPE_BF16)
+    return fail(kErrInvalid, "layer_norm: gamma/beta dtype must be f32 or bf16 (got %d)", param_dtype);
+  return layer_norm_launch(x, rows, cols, ldx, gamma, beta, param_dtype == NPUB200_DTYPE_F32 ? 1 : 0, eps, out, ldo,
+                           static_cast<cudaStream_t>(stream));
+}
+
 int npub200_group_norm_scratch_size(int64_t n, int64_t groups, size_t* bytes_out) {
   if (bytes_out == nullptr) return fail(kErrInvalid, "null output pointer");
   if (n <= 0 || groups <= 0) return fail(kErrInvalid, "group_norm sizes must be positive");

@@ -114,6 +114,10 @@ int conv3x3_launch(const ConvProblem& p, cudaStream_t stream);
 size_t group_norm_scratch_bytes(int64_t n, int64_t groups);
 int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t groups, const float* gamma,
                       const float* beta, float eps, int apply_silu, void* out, float* stats, cudaStream_t stream);
+// LayerNorm over the last dimension of bf16 rows: x [rows][ldx], out [rows][ldo] (cols valid); gamma, beta [cols]
+// in f32 (param_f32) or bf16.
+int layer_norm_launch(const void* x, int64_t rows, int64_t cols, int64_t ldx, const void* gamma, const void* beta,
+                      int param_f32, float eps, void* out, int64_t ldo, cudaStream_t stream);
 // Split-K workspace bytes the convolution's fastest plan uses (0: none).
 size_t conv3x3_workspace_bytes(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant, int sms);
 // bf16 copy of a row-strided matrix into a dense [rows, cols_pad] buffer, zero-filling the pad columns.

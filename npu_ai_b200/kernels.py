@@ -267,6 +267,40 @@ def group_norm(x: torch.Tensor, groups: int, gamma: torch.Tensor, beta: torch.Te
     return out
 
 
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """LayerNorm over the last dimension of a bf16 tensor whose rows are evenly strided (contiguous, or a 2-D view
+    with unit column stride); weight, bias: [C] bf16 or f32 on the device. Returns bf16 shaped like x."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or x.dim() < 1:
+        raise ValueError("layer_norm takes a bf16 tensor")
+    C = x.shape[-1]
+    if x.is_contiguous():
+        x2 = x.reshape(-1, C)
+    elif x.dim() == 2 and x.stride(1) == 1:
+        x2 = x
+    else:
+        raise ValueError("layer_norm needs rows with a unit column stride and one row stride")
+    if weight.shape != (C,) or bias.shape != (C,) or weight.dtype != bias.dtype or \
+            weight.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("weight and bias must be [C] tensors of one dtype, bf16 or f32")
+    weight = weight.detach().to(x.device).contiguous()
+    bias = bias.detach().to(x.device).contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    if out.shape != x.shape or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 tensor shaped like x")
+    rows = x2.shape[0]
+    if rows == 0:
+        return out
+    with torch.cuda.device(x.device):
+        _lib.call("npub200_layer_norm", ctypes.c_void_p(x2.data_ptr()), rows, C, x2.stride(0),
+                  ctypes.c_void_p(weight.data_ptr()), ctypes.c_void_p(bias.data_ptr()),
+                  _lib.DTYPE_F32 if weight.dtype == torch.float32 else _lib.DTYPE_BF16, ctypes.c_float(eps),
+                  ctypes.c_void_p(out.data_ptr()), C, ctypes.c_void_p(_stream_ptr(x.device)))
+    return out
+
+
 def _bshd_strides(t: torch.Tensor, head_major: bool) -> tuple[int, int, int]:
     """(batch, seq, head) element strides of a (B, S, H, D) view given as (B, S, H*D) or (B, H, S, D)."""
     if head_major:

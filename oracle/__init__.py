@@ -23,4 +23,4 @@ accuracy figures (docs/02-results.md:709) that the attention oracle reproduces o
 inputs; see tests/test_oracle.py.
 """
 from .reference_ops import (attention_ref, bf16_round, conv3x3_ref, cosine, geglu_ref,  # noqa: F401
-                            group_norm_ref, linear_ref, rel_l2_err, rel_max_err)
+                            group_norm_ref, layer_norm_ref, linear_ref, rel_l2_err, rel_max_err)

@@ -61,6 +61,13 @@ def group_norm_ref(x_nhwc: torch.Tensor, groups: int, gamma: torch.Tensor, beta:
     return y.permute(0, 2, 3, 1)
 
 
+def layer_norm_ref(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """f32 `F.layer_norm` over the last dimension of a bf16-rounded tensor: the host-side norm1/norm2/norm3 of a
+    transformer block around the reference's offloaded projections (docs/02-results.md:411-413)."""
+    x = bf16_round(x)
+    return F.layer_norm(x, (x.shape[-1],), gamma.detach().to("cpu").float(), beta.detach().to("cpu").float(), eps)
+
+
 def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
                   head_major: bool = False) -> torch.Tensor:
     """f32 softmax(bf16(q) bf16(k)^T * scale) bf16(v) for every (batch, head) pair.

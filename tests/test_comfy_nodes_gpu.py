@@ -79,6 +79,7 @@ def test_offload_node_end_to_end(cuda_device, unet_pair):
     # 16 self-attention q/k/v groups + one grouped GEMM for all 16 cross-attention k/v pairs (shared context)
     assert len(rt.fused_groups) == 17, len(rt.fused_groups)
     assert len(rt.tblocks) == 16, len(rt.tblocks)               # residual adds in the output GEMMs' epilogues
+    assert len(rt.lnorms) == 48, len(rt.lnorms)                 # norm1/norm2/norm3 of each block
     assert not rt.pending_res
     assert rt.attn.counts["gpu"] > 0 and rt.attn.decision, "attention never reached the fused kernel"
     assert all(e <= 0.1 for e in rt.attn.max_err.values())
