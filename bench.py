@@ -59,7 +59,7 @@ def _peaks() -> dict:
 
 # DRAM traffic per launch of the dominant kernel (GEMM, averaged over the 66 sweep launches) from the committed
 # ncu capture summarised in profiles/gemm_sweep_dram.md (mean over the 66 launches of one step).
-GEMM_DRAM_BYTES_PER_LAUNCH = 15834868
+GEMM_DRAM_BYTES_PER_LAUNCH = 14401380
 
 
 # ----------------------------------------------------------------------------------------------------------------
