@@ -56,12 +56,10 @@ struct GemmArgs {
   long long ldo;
   int out_f32;
   int tma_store;  // 1: the output goes out through TMA stores (aligned output), 0: direct predicated stores
-  // Split-K: `splits` CTAs share an output tile, each over `kb_per_split` K blocks; f32 partials go to
-  // `ws_partial` ([tile][split][column][row]) and the last to arrive (ticket from `ws_counter[tile]`, which it
-  // resets to 0) sums them in split order, so the result does not depend on arrival order.
+  // Split-K: `splits` CTAs, one cluster, share an output tile, each over `kb_per_split` K blocks. Each parks its
+  // f32 partial in its own shared memory; after all have, each sums a slice of the tile over every CTA's partial
+  // in split order (distributed shared memory), so the result does not depend on timing.
   int splits, kb_per_split;
-  float* ws_partial;
-  unsigned int* ws_counter;
   KernelCtl ctl;
 };
 
@@ -76,8 +74,8 @@ struct GemmLayout {
   static constexpr int kStagingOffset = STAGES * kStageBytes;
   static constexpr int kStagingBytes = kGemmEpiWarps * 32 * 128;
   static constexpr int kBarOffset = kStagingOffset + kStagingBytes;
-  // full[S], empty[S], acc_full[2], acc_empty[2], drain, bias_full, bias_free
-  static constexpr int kNumBars = 2 * STAGES + 7;
+  // full[S], empty[S], acc_full[2], acc_empty[2], drain, bias_full, bias_free, parts_ready
+  static constexpr int kNumBars = 2 * STAGES + 8;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   // The tile's bias in f32 (BN entries: the output columns', then in the GEGLU form the gate columns').
   static constexpr int kBiasOffset = (kMiscOffset + 16 + 15) / 16 * 16;
@@ -128,6 +126,13 @@ __device__ __forceinline__ void load_bias32(const GemmArgs& a, int gcol, float (
       for (int j = 0; j < 32; ++j) b[j] = (gcol + j < a.bias_n) ? __bfloat162float(p[j]) : 0.0f;
     }
   }
+}
+
+// Bias of column gcol + j for one row (row_off: that row's bias row), 0 beyond bias_n or without a bias.
+__device__ __forceinline__ float load_bias_own(const GemmArgs& a, int gcol, int j, long long row_off) {
+  if (a.bias == nullptr || gcol + j >= a.bias_n) return 0.0f;
+  return a.bias_f32 ? __ldg(static_cast<const float*>(a.bias) + row_off + gcol + j)
+                    : __bfloat162float(static_cast<const __nv_bfloat16*>(a.bias)[row_off + gcol + j]);
 }
 
 // Direct-store epilogue for outputs TMA cannot address: 32 columns of one row, rows/columns predicated with
@@ -285,6 +290,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = acc_empty + 2;
   uint64_t* bias_full = drain + 1;  // the epilogue warps have written this tile's bias table
   uint64_t* bias_free = drain + 2;  // the epilogue warps are done reading the previous tile's table
+  uint64_t* parts_ready = drain + 3;  // split K: every CTA of the cluster has parked its partial tile
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
 
@@ -303,6 +309,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(drain, 1);
     mbar_init(bias_full, kGemmEpiThreads);  // one arrival per epilogue thread
     mbar_init(bias_free, kGemmEpiThreads);
+    mbar_init(parts_ready, uint32_t(args.splits));  // one arrival from each CTA of a split-K cluster
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -320,8 +327,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     tc_fence_before();
   }
-  // A pair's barriers must be initialised in both CTAs before either CTA's copies or commits reach them.
-  if constexpr (PAIR)
+  // A pair's (or split-K cluster's) barriers must be initialised in every CTA before another CTA's copies, commits
+  // or arrivals reach them.
+  const bool clustered = PAIR || (!GEGLU && args.splits > 1);  // the GEGLU form never splits K
+  if (clustered)
     cluster_sync();
   else
     __syncthreads();
@@ -505,7 +514,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // alternate chunks. A chunk that would reach past the tile (BN not a multiple of the chunk) is written with
     // direct stores instead.
     uint8_t* sb = smem + L::kStagingOffset + (warp - 2) * (32 * 128);
-    volatile int* last_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 8);
     const int cw = args.out_f32 ? 32 : 64;
     const int splits = args.splits;
     int local = 0;
@@ -555,29 +563,87 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.ctl, kStatusTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
-      bool emit = true;
       if (!GEGLU && splits > 1) {
-        // Publish this split's partial, then take a ticket; the last split of the tile reduces.
-        float* mine = args.ws_partial + (size_t(tile) * splits + split) * BN * kGemmBM;
+        // Split K over the CTAs of this cluster (one per split, launched together): park this split's partial tile
+        // in shared memory ([row][BN + 4] f32; the operand ring is idle once the accumulator is complete, and a
+        // split-K CTA has no further unit), tell every CTA of the cluster, wait for all of them, then sum this CTA's
+        // slice of rows over every CTA's partial in split order through distributed shared memory and store it.
+        constexpr int kPS = BN + 4;
+        float* part = reinterpret_cast<float*>(smem);
 #pragma unroll 1
         for (int c = half * 32; c < BN; c += 64) {
           uint32_t r[32];
           tmem_ld32(t_row + uint32_t(c), r);
           tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(part + row * kPS + c);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) __stcg(mine + (c + j) * kGemmBM + row, __uint_as_float(r[j]));
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
         }
-        __threadfence();
         named_barrier_sync(1, kGemmEpiThreads);
         if (threadIdx.x == 64) {
-          const unsigned int ticket = atomicAdd(args.ws_counter + tile, 1u);
-          *last_flag = (ticket == unsigned(splits - 1)) ? 1 : 0;
+          fence_acq_rel_cluster();
+          for (int s2 = 0; s2 < splits; ++s2) mbar_arrive_cluster(cluster_smem_addr(parts_ready, uint32_t(s2)));
         }
-        named_barrier_sync(1, kGemmEpiThreads);
-        emit = *last_flag != 0;
-        __threadfence();
-      }
-      if (emit) {
+        if (!mbar_wait_cluster_bounded(parts_ready, 0u, abort_flag, args.ctl, kStatusTimeoutEpilogue)) break;
+        const int r0 = (kGemmBM * split) / splits;
+        const int r1 = (kGemmBM * (split + 1)) / splits;
+        const int items = (r1 - r0) * (BN / 4);
+#pragma unroll 1
+        for (int it = int(threadIdx.x) - 64; it < items; it += kGemmEpiThreads) {
+          const int rr = r0 + it / (BN / 4);
+          const int cc = (it % (BN / 4)) * 4;
+          const float* mine = part + rr * kPS + cc;
+          float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+          for (int s2 = 0; s2 < splits; ++s2) {
+            const float4 p4 = ld_cluster_f32x4(cluster_smem_addr(mine, uint32_t(s2)));
+            v[0] += p4.x;
+            v[1] += p4.y;
+            v[2] += p4.z;
+            v[3] += p4.w;
+          }
+          const int grow = m0 + rr;
+          const int gcol = n0 + cc;
+          if (grow >= args.M || gcol >= args.N) continue;
+          const long long own =
+              args.bias_img_stride > 0
+                  ? (long long)min(grow / args.bias_img_pixels, args.bias_imgs - 1) * args.bias_img_stride
+                  : 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float b = 0.f;
+            if (table_bias)
+              b = bias_tab[cc + j];
+            else
+              b = load_bias_own(args, gcol, j, own);
+            v[j] += b;
+            if (args.residual != nullptr && gcol + j < args.N)
+              v[j] += __bfloat162float(static_cast<const __nv_bfloat16*>(args.residual)[(long long)grow * args.ldr +
+                                                                                          gcol + j]);
+          }
+          if (args.out_f32) {
+            float* o = static_cast<float*>(args.out) + (long long)grow * args.ldo + gcol;
+            if (gcol + 4 <= args.N && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+              *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                if (gcol + j < args.N) o[j] = v[j];
+            }
+          } else {
+            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(args.out) + (long long)grow * args.ldo + gcol;
+            if (gcol + 4 <= args.N && (reinterpret_cast<uintptr_t>(o) & 7) == 0) {
+              *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                if (gcol + j < args.N) o[j] = __float2bfloat16_rn(v[j]);
+            }
+          }
+        }
+      } else {
 #pragma unroll 1
         for (int c0 = half * cw; c0 < kOutCols; c0 += 2 * cw) {
           const bool chunk_tma = args.tma_store && c0 + cw <= kOutCols;
@@ -608,46 +674,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             };
             float v[32];
             if constexpr (GEGLU) {
+              // The GEGLU form has one bias row (or none): its table holds the a-columns' then the gate columns'.
               uint32_t r[32], rg[32];
               tmem_ld32(t_row + uint32_t(c), r);
               tmem_ld32(t_row + uint32_t(kOutCols + c), rg);
-              float b[32], bg[32];
-              fetch_bias(b, c, n0 + c);
-              if (table_bias) {
-                fetch_bias(bg, kOutCols + c, 0);
-              } else {
-                load_bias32(args, args.N + n0 + c, bg);  // gate columns: one bias row
-              }
               tmem_wait_ld();
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                v[j] = (__uint_as_float(r[j]) + b[j]) * gelu_erf(__uint_as_float(rg[j]) + bg[j]);
-            } else {
-              if (splits > 1) {
-                // Fixed summation order over the splits, every partial (this split's own too, published above)
-                // read back from L2. Each pass costs a round trip there, so two splits' loads go out per pass.
-                const float* part0 = args.ws_partial + size_t(tile) * splits * BN * kGemmBM + c * kGemmBM + row;
-                const size_t slab = size_t(BN) * kGemmBM;
+              for (int j4 = 0; j4 < 8; ++j4) {
+                const float4 b4 = table_bias ? reinterpret_cast<const float4*>(bias_tab + c)[j4]
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 g4 = table_bias ? reinterpret_cast<const float4*>(bias_tab + kOutCols + c)[j4]
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+                const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = 0.0f;
-#pragma unroll 1
-                for (int sp = 0; sp < splits; sp += 2) {
-                  float p0[32], p1[32];
-                  const bool two = sp + 1 < splits;
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) p0[j] = __ldcg(part0 + sp * slab + j * kGemmBM);
-                  if (two) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) p1[j] = __ldcg(part0 + (sp + 1) * slab + j * kGemmBM);
-                  }
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) v[j] += p0[j];
-                  if (two) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] += p1[j];
-                  }
+                for (int e = 0; e < 4; ++e) {
+                  const int j = 4 * j4 + e;
+                  v[j] = (__uint_as_float(r[j]) + bb[e]) * gelu_erf(__uint_as_float(rg[j]) + gg[e]);
                 }
-              } else {
+              }
+            } else {
+              {
                 uint32_t r[32];
                 tmem_ld32(t_row + uint32_t(c), r);
                 tmem_wait_ld();
@@ -695,7 +742,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-        if (!GEGLU && splits > 1 && threadIdx.x == 64) args.ws_counter[tile] = 0u;  // leave the counter zeroed for reuse
       }
       tc_fence_before();
       __syncwarp();
@@ -710,8 +756,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (args.tma_store && lane == 0) bulk_wait_read<0>();  // staging must not be released while being read
   }
 
-  // Nothing of either CTA of a pair may be freed while the other can still reach it.
-  if constexpr (PAIR)
+  // Nothing of a CTA of a pair or split-K cluster (its barriers, its parked partial) may go while another CTA of the
+  // cluster can still reach it.
+  if (clustered)
     cluster_sync();
   else
     __syncthreads();
@@ -729,23 +776,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ---------------------------------------------------------------------------------------------------------------
 namespace {
 
-// Launch one instantiation as a persistent grid over `units` work units: one CTA per SM, or for a pair variant one
-// two-CTA cluster per SM pair (as many clusters as can be resident at once, from the occupancy query).
+// Launch one instantiation over `units` work units: a persistent grid of one CTA per SM; for a pair variant one
+// two-CTA cluster per SM pair (as many as can be resident at once, from the occupancy query); for split K one
+// cluster of `splits` CTAs per output tile, one unit per CTA.
 template <int BN, int STAGES, int MODE = kModePlain, bool PAIR = false>
 int launch_variant(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mo, const GemmArgs& args,
                    int64_t units, int sms, cudaStream_t st, int device) {
   using L = GemmLayout<BN, STAGES, PAIR ? BN / 2 : BN>;
   static bool configured[64] = {false};
-  static int resident_clusters[64] = {0};
+  static int resident_clusters[64][kGemmMaxSplits + 1] = {};
   auto kern = gemm_bf16_tcgen05_kernel<BN, STAGES, MODE, PAIR>;
   if (device < 0 || device >= 64) return fail(kErrInvalid, "device ordinal %d out of range", device);
+  const int cluster = PAIR ? 2 : args.splits;
+  if (cluster < 1 || cluster > kGemmMaxSplits) return fail(kErrInvalid, "GEMM cluster of %d CTAs", cluster);
+  if (PAIR && args.splits != 1) return fail(kErrInvalid, "paired GEMM tiles do not split K");
   if (!configured[device]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm smem)");
-    if (PAIR) {
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
-      if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm cluster)");
-    }
     configured[device] = true;
   }
   cudaLaunchConfig_t cfg;
@@ -757,23 +804,27 @@ int launch_variant(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorM
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.x = unsigned(cluster);
   attr[1].val.clusterDim.y = 1;
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = PAIR ? 2 : 1;
-  int grid = int(std::min<int64_t>(units, sms));
-  if (PAIR) {
-    if (resident_clusters[device] == 0) {
-      cfg.gridDim = dim3(unsigned(2 * (sms / 2)));
+  cfg.numAttrs = cluster > 1 ? 2 : 1;
+  int64_t grid = std::min<int64_t>(units, sms);
+  if (cluster > 1) {
+    int& resident = resident_clusters[device][cluster];
+    if (resident == 0) {
+      cfg.gridDim = dim3(unsigned(cluster * (sms / cluster)));
       int n = 0;
       cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
       if (e != cudaSuccess) return check_cuda(e, "cudaOccupancyMaxActiveClusters(gemm)");
-      if (n < 1) return fail(kErrUnsupported, "no two-CTA cluster of the GEMM fits on this device");
-      resident_clusters[device] = n;
+      if (n < 1) return fail(kErrUnsupported, "no %d-CTA cluster of the GEMM fits on this device", cluster);
+      resident = n;
     }
-    grid = 2 * int(std::min<int64_t>(units, resident_clusters[device]));
+    // Pairs: persistent over units. Split K: every unit gets its own CTA (the clusters beyond the resident ones
+    // start as others finish).
+    grid = PAIR ? 2 * std::min<int64_t>(units, resident) : units;
   }
+  if (grid > INT32_MAX) return fail(kErrInvalid, "GEMM grid too large");
   cfg.gridDim = dim3(unsigned(grid));
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, mx, mw, mo, args), "gemm kernel launch");
 }
@@ -814,15 +865,12 @@ constexpr int kTileChoices[] = {64, 96, 128, 160, 192, 256};
 }  // namespace
 
 namespace {
-// Split-K tile counters live in a fixed region at the start of the workspace (split-K only runs when the tiles
-// number at most half the SMs), so a workspace reused across problems always finds them at the same place.
-constexpr size_t kSplitCounterBytes = 4096;
 
 // Modelled time (SM clocks) of a plan: waves of persistent work units x per-unit time. A unit's main loop is
 // bounded by the larger of the tensor-core time (2*BN clocks per 64-deep K block at 8192 FLOP/clk/SM) and the
 // time to stream its operands into shared memory (~64 B/clk/SM); each unit pays a fixed pipeline fill. A split
-// tile pays for publishing its f32 partial and for the last split's reduction, which is latency-bound: each
-// epilogue warp reduces BN/64 groups of 32 columns, one L2 round trip (~1050 clocks measured) per two splits.
+// tile pays for parking its f32 partial in shared memory, the cluster hand-off, and its slice of the reduction
+// over the cluster's partials (distributed shared memory).
 double plan_cost(int64_t M, int64_t N, int64_t kb, int bn, int splits, int sms) {
   const int64_t tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + bn - 1) / bn);
   const int64_t units = tiles * splits;
@@ -831,7 +879,7 @@ double plan_cost(int64_t M, int64_t N, int64_t kb, int bn, int splits, int sms) 
   const double mma = 2.0 * bn;
   const double load = (kGemmBM + bn) * 128.0 / 64.0;
   double t = double(kb_unit) * std::max(mma, load) + 1500.0 + 8.0 * bn;
-  if (splits > 1) t += 1000.0 + (bn / 64.0) * (600.0 + 1050.0 * double((splits + 1) / 2));
+  if (splits > 1) t += 4000.0 + 12.0 * bn + 150.0 * splits;
   return double(waves) * t;
 }
 }  // namespace
@@ -863,6 +911,39 @@ bool gemm_variant_known(int variant, bool geglu) {
   return known && (!pair || pair_tile(bn)) && (!geglu || bn % 64 == 0);
 }
 
+int gemm_cluster_slots(int size) {
+  static int slots[64][kGemmMaxSplits + 1] = {};
+  if (size < 2 || size > kGemmMaxSplits) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (slots[dev][size] == 0) {
+    // Every GEMM instantiation holds one CTA per SM (more than half of the shared memory), so one stands for all.
+    using L = GemmLayout<64, 8>;
+    auto kern = gemm_bf16_tcgen05_kernel<64, 8, kModePlain, false>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes) != cudaSuccess)
+      return 0;
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = L::kSmemBytes;
+    cfg.gridDim = dim3(unsigned(size * 16));
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(size);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return 0;
+    }
+    slots[dev][size] = n > 0 ? n : -1;
+  }
+  return std::max(slots[dev][size], 0);
+}
+
 GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool geglu, bool auto_pair) {
   // N counts accumulator columns: for the GEGLU form the 2 x inner projection columns, and only tiles with an even
   // split into a and gate halves of 32-column multiples are candidates. `variant` (when not 0) forces one tile:
@@ -877,19 +958,22 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool g
     // Split K only when the tiles leave most SMs idle and each split keeps >= 4 K blocks (never for GEGLU, whose
     // gating needs the finished sums).
     int max_split = 1;
-    if (!geglu && tiles * 2 <= sms && tiles * 4 <= int64_t(kSplitCounterBytes) && kb >= 8)
-      max_split = int(std::min<int64_t>(std::min<int64_t>(sms / tiles, kb / 4), 16));
+    if (!geglu && tiles * 2 <= sms && kb >= 8)
+      max_split = int(std::min<int64_t>(std::min<int64_t>(sms / tiles, kb / 4), kGemmMaxSplits));
     for (int sp = 1; sp <= max_split; ++sp) {
       const int kps = int((kb + sp - 1) / sp);
       const int eff = int((kb + kps - 1) / kps);  // splits actually needed with kps blocks each
       if (eff != sp) continue;
+      // A split plan runs as tiles clusters of sp CTAs; clusters are placed within a GPC, so only as many as
+      // gemm_cluster_slots(sp) run at once. Plans needing a second wave of clusters are not taken.
+      if (sp > 1 && tiles > gemm_cluster_slots(sp)) continue;
       const double cost = plan_cost(M, N, kb, bn, sp, sms);
       if (cost < best_cost * 0.999 || (cost <= best_cost * 1.001 && bn > best.bn && sp <= best.splits)) {
         best_cost = cost;
         best.bn = bn;
         best.splits = sp;
         best.kb_per_split = kps;
-        best.split_ws_bytes = sp > 1 ? kSplitCounterBytes + size_t(tiles) * sp * bn * kGemmBM * 4 : 0;
+        best.split_ws_bytes = 0;  // split K reduces through distributed shared memory: no workspace
       }
     }
   }
@@ -926,11 +1010,6 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   GemmPlan plan = gemm_plan(p.M, geglu ? 2 * p.N : p.N, p.K, dev->sms, p.variant, geglu);
   const int bn = plan.bn;
   const int out_cols = geglu ? bn / 2 : bn;  // output columns per tile
-  if (plan.splits > 1 && (p.ws_split == nullptr || p.ws_split_bytes < plan.split_ws_bytes ||
-                          (reinterpret_cast<uintptr_t>(p.ws_split) & 255) != 0)) {
-    plan.splits = 1;  // no room for partials: one CTA per tile over all of K
-    plan.kb_per_split = int((p.K + kGemmBK - 1) / kGemmBK);
-  }
 
   CUtensorMap mx, mw;
   if (int rc = encode_kmajor_map(p.x, p.M, p.K, p.ldx, kGemmBM, &mx)) return rc;
@@ -974,9 +1053,6 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.out_f32 = p.out_f32;
   a.splits = plan.splits;
   a.kb_per_split = plan.kb_per_split;
-  a.ws_counter = plan.splits > 1 ? static_cast<unsigned int*>(p.ws_split) : nullptr;
-  a.ws_partial =
-      plan.splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(p.ws_split) + kSplitCounterBytes) : nullptr;
   a.ctl.status = dev->status;
   a.ctl.timeout_ns = wait_timeout_ns();
   a.ctl.debug = p.debug;
@@ -1053,11 +1129,6 @@ int conv3x3_launch(const ConvProblem& p, cudaStream_t stream) {
   GemmPlan plan = gemm_plan(M, p.cout, K, dev->sms, p.variant, false, false);
   const int bn = plan.bn;
   const int tile_m = plan.pair ? 2 * kGemmBM : kGemmBM;
-  if (plan.splits > 1 && (p.ws_split == nullptr || p.ws_split_bytes < plan.split_ws_bytes ||
-                          (reinterpret_cast<uintptr_t>(p.ws_split) & 255) != 0)) {
-    plan.splits = 1;  // no room for partials: one CTA per tile over all of K
-    plan.kb_per_split = int(K / kGemmBK);
-  }
 
   EncodeTiledFn enc = nullptr;
   if (int rc = encode_tiled_fn(&enc)) return rc;
@@ -1102,9 +1173,6 @@ int conv3x3_launch(const ConvProblem& p, cudaStream_t stream) {
   a.out_f32 = p.out_f32;
   a.splits = plan.splits;
   a.kb_per_split = plan.kb_per_split;
-  a.ws_counter = plan.splits > 1 ? static_cast<unsigned int*>(p.ws_split) : nullptr;
-  a.ws_partial =
-      plan.splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(p.ws_split) + kSplitCounterBytes) : nullptr;
   a.cv_w = int(p.w);
   a.cv_hw = int(p.h * p.w);
   a.cv_cblocks = int(p.cin / kGemmBK);

@@ -55,7 +55,7 @@ struct GemmProblem {
   int64_t M, N, K;
   int variant;       // 0 = automatic, else a forced N tile (64, 96, 128, 160, 192, 256)
   const CUtensorMap* w_map_cache;  // optional cached B tensor map (matching the chosen tile), may be null
-  void* ws_split;                  // split-K workspace: zeroed counters, then f32 partials (may be null)
+  void* ws_split;                  // caller workspace (split K needs none: it reduces inside a cluster)
   size_t ws_split_bytes;
   uint32_t debug;
   int geglu;  // 1: W has 2N rows [a; gate] and out[:, j] = (x.W[j] + b[j]) * gelu(x.W[N+j] + b[N+j]); bias has 2N
@@ -67,11 +67,15 @@ struct GemmPlan {
   int bn;
   int splits;
   int kb_per_split;
-  size_t split_ws_bytes;  // bytes of split-K workspace the plan needs (0 when splits == 1)
+  size_t split_ws_bytes;  // bytes of split-K workspace the plan needs (0: split K reduces inside a cluster)
   bool pair;              // 256-row tiles on a two-CTA cluster (tcgen05 cta_group::2)
 };
 // Tile variants: BN (64 ... 256) for one CTA per tile, kGemmPairVariant + BN (128, 192, 256) for a CTA pair.
 constexpr int kGemmPairVariant = 1000;
+// Split K runs the splits of a tile as one cluster (the portable cluster size bounds it).
+constexpr int kGemmMaxSplits = 8;
+// Clusters of `size` one-CTA-per-SM GEMM CTAs that can be resident at once on the current device (0: unknown).
+int gemm_cluster_slots(int size);
 bool gemm_variant_known(int variant, bool geglu);
 // auto_pair: whether the automatic choice (variant 0) may pick a pair tile.
 GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int variant, bool geglu = false, bool auto_pair = true);
@@ -105,7 +109,7 @@ struct ConvProblem {
   int out_f32;
   int variant;                // 0 or a forced output-channel tile
   uint32_t debug;
-  void* ws_split;             // split-K workspace (zeroed counters, then f32 partials), may be null
+  void* ws_split;             // caller workspace (split K needs none: it reduces inside a cluster)
   size_t ws_split_bytes;
 };
 int conv3x3_launch(const ConvProblem& p, cudaStream_t stream);

@@ -214,6 +214,43 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
+// Wait on a phase of this CTA's mbarrier with acquire semantics at cluster scope (arrivals released by other CTAs
+// of the cluster, and the shared-memory writes before them, are visible after). Bounded like mbar_wait_bounded.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+static __device__ __noinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                              const KernelCtl& ctl, uint32_t code) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 31u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > ctl.timeout_ns) {
+        *abort = 1;
+        atomicOr(ctl.status, code);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
 // Every thread of both CTAs: shared-memory writes (barrier inits included) before it are visible to the pair after.
 // The non-.aligned forms, so threads of a warp may reach it at different times (roles run on single lanes).
 __device__ __forceinline__ void cluster_sync() {

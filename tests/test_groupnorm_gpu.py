@@ -8,9 +8,10 @@ from test_gemm_gpu import _check_bf16
 
 pytestmark = pytest.mark.gpu
 
-# (n, h, w, c): the SD1.5 ResBlock widths (group sizes 10, 20, 30, 40, 60, 80 channels) at batch 2 and 16.
+# (n, h, w, c): the SD1.5 ResBlock widths (group sizes 10, 20, 30, 40, 60, 80 channels) at batch 2 (two kernels)
+# and 16 (>= 4M values: the one-launch cooperative form), and 4608 channels (past its 4096: two kernels).
 SHAPES = [(2, 64, 64, 320), (2, 32, 32, 640), (2, 8, 8, 1280), (2, 16, 16, 1920), (1, 8, 8, 960), (16, 32, 32, 640),
-          (2, 16, 16, 2560)]
+          (2, 16, 16, 2560), (16, 64, 64, 320), (1, 8, 8, 4608)]
 
 
 def _inputs(n, h, w, c, seed=0):
