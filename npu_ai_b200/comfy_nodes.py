@@ -135,6 +135,13 @@ class B200Runtime:
         self.convs: dict[int, tuple] = {}
         self.norms: dict[int, tuple] = {}
         self.resblocks: dict[int, tuple] = {}
+        # Time-embedding projections of the fused ResBlocks, grouped: every ResBlock of a UNet call reads the same
+        # `emb`, so their SiLU + Linear (with the first convolution's bias folded in) run as ONE GEMM per input
+        # width. emb_groups[i] = (fused NpuWeight, f32 bias); emb_slices[id(ResBlock)] = (i, column offset, cout);
+        # emb_cache[i] = (weakref to the emb it was computed for, its version, [n, columns] f32 result).
+        self.emb_groups: list[tuple] = []
+        self.emb_slices: dict[int, tuple] = {}
+        self.emb_cache: dict[int, tuple] = {}
         self.conv_calls = 0  # convolution-side calls that ran on the B200 kernels (ResBlocks count once)
         # Transformer blocks whose residual adds go into the output Linears' GEMM epilogues: id(block) ->
         # (attn1 out Linear, attn2 out Linear, feed-forward out Linear); pending_res: id(Linear) -> residual.
@@ -254,6 +261,25 @@ class B200Runtime:
                 self.resblocks[id(mod)] = plan
                 self.installed[id(mod)] = (mod, mod.forward)
                 mod.forward = types.MethodType(_gpu_resblock_forward, mod)
+        by_width: dict[int, list] = {}
+        for mod in dm.modules():
+            if id(mod) in self.resblocks and id(mod) not in self.emb_slices:
+                by_width.setdefault(mod.emb_layers[1].in_features, []).append(mod)
+        for blocks in by_width.values():
+            lins = [b.emb_layers[1] for b in blocks]
+            w = torch.cat([lin.weight.detach() for lin in lins])
+            parts = []
+            for b, lin in zip(blocks, lins):
+                cb = self.convs[id(self.resblocks[id(b)][1])][2]
+                e = lin.bias.detach().to(dev, torch.float32) if lin.bias is not None else \
+                    torch.zeros(lin.out_features, device=dev)
+                parts.append(e + cb if cb is not None else e)
+            gi = len(self.emb_groups)
+            self.emb_groups.append((self.gemm.upload_weight(w, layout="nk"), torch.cat(parts).contiguous()))
+            off = 0
+            for b, lin in zip(blocks, lins):
+                self.emb_slices[id(b)] = (gi, off, lin.out_features)
+                off += lin.out_features
 
     def _add_group(self, group: list) -> None:
         w = torch.cat([m.weight.detach() for m in group])
@@ -280,6 +306,11 @@ class B200Runtime:
         for kind, wt, _ in self.convs.values():
             if kind == "1x1":
                 wt.release()
+        for nw, _ in self.emb_groups:
+            nw.release()
+        self.emb_groups.clear()
+        self.emb_slices.clear()
+        self.emb_cache.clear()
         self.convs.clear()
         self.norms.clear()
         self.lnorms.clear()
@@ -505,6 +536,24 @@ def _resblock_plan(mod, rt):
     return (il[0], conv1, ol[0], conv2, skip)
 
 
+def _resblock_emb_rows(rt, block, emb, conv1) -> torch.Tensor:
+    """conv1's per-image bias rows, emb_layers(emb) + conv1.bias in f32: a column slice of the grouped projection of
+    all ResBlocks, computed by the first ResBlock that sees this `emb` tensor (identity and version checked)."""
+    ent = rt.emb_slices.get(id(block))
+    if ent is None or not isinstance(emb, torch.Tensor) or not emb.is_cuda:
+        e = block.emb_layers(emb).float()
+        b1 = rt.convs[id(conv1)][2]
+        return (e + b1 if b1 is not None else e).contiguous()
+    gi, off, cout = ent
+    cached = rt.emb_cache.get(gi)
+    if cached is None or cached[0]() is not emb or cached[1] != emb._version:
+        nw, bias = rt.emb_groups[gi]
+        e_all = rt.gemm.linear(torch.nn.functional.silu(emb), nw, bias, out_dtype=torch.float32)
+        cached = (weakref.ref(emb), emb._version, e_all)
+        rt.emb_cache[gi] = cached
+    return cached[2][:, off:off + cout]
+
+
 def _gpu_resblock_forward(self, x, emb, *args, **kwargs):
     """ResBlock.forward in four launches plus the small time-embedding Linear: GroupNorm+SiLU, conv1 with the
     bias row of each image = conv bias + emb_layers(emb), GroupNorm+SiLU, conv2 with the skip path (x or its 1x1
@@ -522,9 +571,7 @@ def _gpu_resblock_forward(self, x, emb, *args, **kwargs):
     t1 = torch.empty_like(xh)
     g1 = rt.norms[id(gn1)]
     kernels.group_norm(xh, gn1.num_groups, g1[0], g1[1], eps=gn1.eps, silu=True, out=t1)
-    e = self.emb_layers(emb).float()
-    b1 = rt.convs[id(conv1)][2]
-    rows = (e + b1 if b1 is not None else e).contiguous()  # [n, cout]: conv bias + time embedding per image
+    rows = _resblock_emb_rows(rt, self, emb, conv1)  # [n, cout] f32: conv bias + time embedding per image
     cout = conv1.out_channels
     h1 = torch.empty((n, h, w, cout), dtype=torch.bfloat16, device=x.device)
     kernels.conv3x3(t1, rt.convs[id(conv1)][1], rows, out=h1)

@@ -190,8 +190,8 @@ def conv3x3(x: torch.Tensor, w_packed: torch.Tensor, bias: torch.Tensor | None =
     """3x3 convolution (stride 1, zero padding 1) as an implicit GEMM, NHWC in and out.
 
     x: bf16 [n, h, w, cin] contiguous (an NCHW channels_last tensor's `.permute(0, 2, 3, 1)` is such a view);
-    w_packed: from pack_conv3x3_weight; bias: [cout] or [n, cout] (one row per image), f32 or bf16; residual: bf16
-    [n, h, w, cout] added after the bias. Returns [n, h, w, cout].
+    w_packed: from pack_conv3x3_weight; bias: [cout] or [n, cout] (one row per image, rows may be strided), f32 or
+    bf16; residual: bf16 [n, h, w, cout] added after the bias. Returns [n, h, w, cout].
     """
     _require_cuda(x, "x")
     if x.dtype != torch.bfloat16 or w_packed.dtype != torch.bfloat16:
@@ -209,9 +209,10 @@ def conv3x3(x: torch.Tensor, w_packed: torch.Tensor, bias: torch.Tensor | None =
         raise ValueError("out must be [n, h, w, cout] with uniformly strided pixel rows")
     img_stride = 0
     if bias is not None:
-        if bias.dtype not in _DT or not bias.is_contiguous() or tuple(bias.shape) not in ((cout,), (n, cout)):
-            raise ValueError("bias must be a contiguous [cout] or [n, cout] f32/bf16 tensor")
-        img_stride = cout if bias.dim() == 2 else 0
+        if bias.dtype not in _DT or tuple(bias.shape) not in ((cout,), (n, cout)) or bias.stride(-1) != 1 or \
+                (bias.dim() == 2 and bias.stride(0) < cout):
+            raise ValueError("bias must be a [cout] or [n, cout] f32/bf16 tensor with unit column stride")
+        img_stride = bias.stride(0) if bias.dim() == 2 else 0
     ldr = 0
     if residual is not None:
         if residual.dtype != torch.bfloat16 or tuple(residual.shape) != (n, h, wd, cout) or residual.stride(-1) != 1 \

@@ -198,6 +198,9 @@ def test_unet_channels_last_on_conv_kernels(cuda_device):
         rt = cn._RUNTIME
         assert len(rt.resblocks) == 22, len(rt.resblocks)
         assert rt.conv_calls > 22, rt.conv_calls
+        # all 22 time-embedding projections in one grouped GEMM per UNet call
+        assert len(rt.emb_slices) == 22 and len(rt.emb_groups) == 1, (len(rt.emb_slices), len(rt.emb_groups))
+        assert len(rt.emb_cache) == 1
         assert torch.isfinite(y).all()
         assert rel_l2_err(y, ref) < 3e-2, rel_l2_err(y, ref)
     finally:
