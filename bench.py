@@ -679,9 +679,17 @@ def run_case(args) -> None:
         # bytes, not FLOPs: one read for the statistics, one read and one write for the apply pass
         fn, flops = (lambda: kernels.group_norm(x, 32, g, bb, silu=True, out=out)), 0.0
         gn_bytes = 3.0 * x.numel() * 2
+    elif kind == "ln":
+        rows, c = d
+        x = _seeded((rows, c), 1.0, 1, device)
+        g, bb = torch.ones(c, device=device), torch.zeros(c, device=device)
+        out = torch.empty_like(x)
+        # bytes: one read and one write of the tensor
+        fn, flops = (lambda: kernels.layer_norm(x, g, bb, out=out)), 0.0
+        gn_bytes = 2.0 * x.numel() * 2
     else:
         raise SystemExit(f"unknown case kind {kind!r} (gemm:M,K,N, attn:B,H,Sq,Skv,D, geglu:M,K,n, "
-                         "conv:n,h,w,cin,cout or gn:n,h,w,c)")
+                         "conv:n,h,w,cin,cout, gn:n,h,w,c or ln:rows,c)")
     for _ in range(args.warmup):
         fn()
     torch.cuda.synchronize()
@@ -695,7 +703,7 @@ def run_case(args) -> None:
     ms = e0.elapsed_time(e1) / args.steps
     print(json.dumps({"case": args.case, "us_per_launch": round(ms * 1e3, 2),
                       "tflops": round(flops / ms / 1e9, 1),
-                      **({"gbs": round(gn_bytes / ms / 1e6, 1)} if kind == "gn" else {})}), flush=True)
+                      **({"gbs": round(gn_bytes / ms / 1e6, 1)} if kind in ("gn", "ln") else {})}), flush=True)
 
 
 def main(argv=None) -> int:
@@ -707,7 +715,7 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--case", default=None, help="time one kernel: gemm:M,K,N, attn:B,H,Sq,Skv,D, geglu:M,K,n, "
-                                                   "conv:n,h,w,cin,cout or gn:n,h,w,c")
+                                                   "conv:n,h,w,cin,cout, gn:n,h,w,c or ln:rows,c")
     ap.add_argument("--workload", choices=["hotpath", "unet"], default="hotpath",
                     help="hotpath: the GEMM sweep + attention blocks (default); unet: SD1.5 UNet denoise steps")
     ap.add_argument("--batch", type=int, default=2, help="unet: images per step, both CFG halves (2 = 1 prompt)")

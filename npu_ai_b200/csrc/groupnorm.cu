@@ -255,17 +255,30 @@ __global__ void __launch_bounds__(kFusedThreads)
   }
   __syncthreads();
   if (!barrier_ok) return;
+  // Group statistics of this image: 16 lanes per group, lane q summing slices q, q + 16, ... (their loads in
+  // flight together), then a fixed 16-lane shuffle tree: one L2 round trip per 16 slices instead of per slice.
   const float cnt = float(hw) * float(cg);
-  for (int g = threadIdx.x; g < groups; g += kFusedThreads) {
+  for (int g0 = 0; g0 < groups; g0 += kFusedThreads / 16) {
+    const int g = g0 + int(threadIdx.x) / 16;
+    const int q = int(threadIdx.x) % 16;
     float a = 0.f, b = 0.f;
-    for (int sl = 0; sl < slices; ++sl) {
-      const float2 pv = __ldcg(&partials[((long long)img * slices + sl) * groups + g]);
-      a += pv.x;
-      b += pv.y;
+    if (g < groups) {
+      for (int sl = q; sl < slices; sl += 16) {
+        const float2 pv = __ldcg(&partials[((long long)img * slices + sl) * groups + g]);
+        a += pv.x;
+        b += pv.y;
+      }
     }
-    const float mean = a / cnt;
-    const float var = fmaxf(b / cnt - mean * mean, 0.f);
-    gst[g] = make_float2(mean, rsqrtf(var + eps));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    if (g < groups && q == 0) {
+      const float mean = a / cnt;
+      const float var = fmaxf(b / cnt - mean * mean, 0.f);
+      gst[g] = make_float2(mean, rsqrtf(var + eps));
+    }
   }
   __syncthreads();
   float2* ab = reinterpret_cast<float2*>(fs);  // [c] (scale, shift), over the spent per-row sums
