@@ -36,6 +36,8 @@ constexpr int kStatsThreads = 256;
 __global__ void __launch_bounds__(kStatsThreads)
     gn_stats_kernel(const __nv_bfloat16* __restrict__ x, int hw, int c, int cg, float eps, float2* __restrict__ stats,
                     float2* __restrict__ partials, unsigned int* __restrict__ counters) {
+  pdl_wait();  // x is the previous kernel's output
+  pdl_launch_dependents();
   const int img = blockIdx.y;
   const int g = blockIdx.x;
   const int slices = gridDim.z;
@@ -121,6 +123,8 @@ __global__ void __launch_bounds__(kApplyThreads)
                     const float2* __restrict__ stats, const float* __restrict__ gamma,
                     const float* __restrict__ beta, int apply_silu) {
   extern __shared__ float2 ab[];  // [c]: (A, B)
+  pdl_wait();  // the statistics kernel's results
+  pdl_launch_dependents();
   const int img = blockIdx.y;
   for (int ch = threadIdx.x; ch < c; ch += kApplyThreads) {
     const float2 st = stats[img * groups + ch / cg];
@@ -388,19 +392,22 @@ int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t g
   const int64_t cg = c / groups;
   int64_t slices = std::max<int64_t>(1, (int64_t(dev->sms) * 4 + n * groups - 1) / (n * groups));
   slices = std::min<int64_t>({slices, int64_t(kGnMaxSlices), std::max<int64_t>(1, hw * cg / 4096)});
-  gn_stats_kernel<<<dim3(unsigned(groups), unsigned(n), unsigned(slices)), kStatsThreads, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(x), int(hw), int(c), int(cg), eps, reinterpret_cast<float2*>(st),
-      reinterpret_cast<float2*>(partials), counters);
-  if (int rc = check_cuda(cudaGetLastError(), "group_norm stats launch")) return rc;
+  if (int rc = check_cuda(launch_pdl(gn_stats_kernel, dim3(unsigned(groups), unsigned(n), unsigned(slices)),
+                                     dim3(kStatsThreads), 0, stream, static_cast<const __nv_bfloat16*>(x), int(hw),
+                                     int(c), int(cg), eps, reinterpret_cast<float2*>(st),
+                                     reinterpret_cast<float2*>(partials), counters),
+                          "group_norm stats launch"))
+    return rc;
   // Pixels per apply block (within one image): about four blocks per SM over the whole tensor, at least one pixel.
   const int64_t vecs = n * hw * (c / 8);
   const int64_t per_block = (vecs + int64_t(dev->sms) * 4 - 1) / (int64_t(dev->sms) * 4);
   const int64_t block_pixels = std::max<int64_t>(1, std::min<int64_t>(hw, (per_block + c / 8 - 1) / (c / 8)));
   const dim3 agrid(unsigned((hw + block_pixels - 1) / block_pixels), unsigned(n));
-  gn_apply_kernel<<<agrid, kApplyThreads, size_t(c) * sizeof(float2), stream>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), int(hw), int(c), int(c / groups),
-      int(groups), int(block_pixels), reinterpret_cast<const float2*>(st), gamma, beta, apply_silu);
-  return check_cuda(cudaGetLastError(), "group_norm apply launch");
+  return check_cuda(launch_pdl(gn_apply_kernel, agrid, dim3(kApplyThreads), size_t(c) * sizeof(float2), stream,
+                               static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), int(hw),
+                               int(c), int(c / groups), int(groups), int(block_pixels),
+                               reinterpret_cast<const float2*>(st), gamma, beta, apply_silu),
+                    "group_norm apply launch");
 }
 
 }  // namespace npub200

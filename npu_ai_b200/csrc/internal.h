@@ -6,10 +6,30 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "sm100_ptx.cuh"
 
 namespace npub200 {
+
+// Launch with programmatic dependent launch allowed: the kernel may start while the previous kernel on the stream
+// finishes, so it must wait (pdl_wait) before touching memory that kernel writes; it lets the next one start early
+// with pdl_launch_dependents.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Error codes returned by the C entry points (mirrored in include/npu_b200.h).
 constexpr int kOk = 0;
