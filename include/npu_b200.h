@@ -59,12 +59,11 @@ int npub200_weight_release(int64_t handle);
  * out f32 or bf16. Replaces NpuGemm.matmul_t (npu/xdna1_gemm.py:349-422) and the GEMM mode of the unified NPU
  * program (npu/xdna1_program.py:451-454, npu/kernels/xdna1_attn.cc:480-574). Any M, N, K >= 1: ragged tails are
  * handled in the kernel. x rows need a 16-byte aligned base and ldx % 8 == 0 (TMA); otherwise x is first
- * repacked into `workspace`. Shapes with few output tiles and a long K split K across CTAs, with f32 partials and
- * per-tile counters in `workspace`. npub200_gemm_workspace_size() gives the bytes the fastest plan uses; its first
- * bytes hold counters that must be ZERO the first time a workspace is used — the kernels leave them zero, so a
- * workspace reused on one stream needs zeroing only once (concurrent calls must not share one). A smaller (or
- * NULL) workspace is accepted when the operands need no repacking: the GEMM then runs without split-K. `variant`
- * 0 picks the tile automatically, or forces an N tile in {64, 96, 128, 160, 192, 256}.
+ * repacked into `workspace`. Shapes with few output tiles and a long K split K across the CTAs of a cluster,
+ * which reduce their partials in shared memory: no workspace. npub200_gemm_workspace_size() gives the bytes a call
+ * needs (repacked operands, else 0); a workspace reused on one stream is fine, concurrent calls must not share one,
+ * and NULL is accepted when the operands need no repacking. `variant` 0 picks the tile automatically, or forces an
+ * N tile in {64, 96, 128, 160, 192, 256}, or 1000 + {128, 192, 256} for 256-row tiles on a two-CTA cluster.
  * ---------------------------------------------------------------------------------------------------------- */
 int npub200_gemm_workspace_size(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw,
                                 int64_t n, int variant, size_t* bytes_out);
@@ -114,9 +113,8 @@ int npub200_conv3x3(const void* x, int64_t n, int64_t h, int64_t w, int64_t cin,
                     const void* bias, int bias_dtype, int64_t bias_img_stride, const void* residual, int64_t ldr,
                     void* out, int64_t ldo, int out_dtype, void* workspace, size_t workspace_bytes, int variant,
                     void* stream);
-/* Workspace bytes npub200_conv3x3 uses to split K across CTAs when the output tiles are too few to fill the GPU
- * (small images, many channels). The same rules as the GEMM's workspace: its first bytes are counters that must be
- * zero when first used and are left zero; NULL or a smaller workspace runs without split-K. */
+/* Workspace bytes npub200_conv3x3 needs: 0 (split K, for small images with many channels, reduces inside a
+ * cluster's shared memory); NULL is accepted. Kept so callers size a workspace the same way as for the GEMM. */
 int npub200_conv3x3_workspace_size(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant,
                                    size_t* bytes_out);
 
@@ -147,8 +145,8 @@ int npub200_layer_norm(const void* x, int64_t rows, int64_t cols, int64_t ldx, c
  * its NPU runner allocates its own pinned buffers. Same arguments and result as npub200_gemm minus the
  * workspace; the scratch is one fixed device array of NPUB200_NOALLOC_SCRATCH_BYTES per GPU, held from library
  * load to process exit, and this call allocates nothing. A shape whose scratch need exceeds the array is rejected
- * with NPUB200_EINVAL. The first call on a device resolves the array and clears its counters (make it before any
- * stream capture). All calls share the array and it keeps the last call's contents: calls that overlap on the GPU
+ * with NPUB200_EINVAL. The first call on a device resolves the array and clears its leading region (make it before
+ * any stream capture). All calls share the array and it keeps the last call's contents: calls that overlap on the GPU
  * (several streams, several host threads) race and must be serialised by the caller, e.g. on one stream.
  * ---------------------------------------------------------------------------------------------------------- */
 #define NPUB200_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)

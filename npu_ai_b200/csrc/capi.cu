@@ -112,9 +112,9 @@ bool tma_rows_ok(const void* p, int64_t ld, int64_t cols) { return aligned16(p) 
 
 int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
-// Workspace layout: [4 KiB split-K tile counters][f32 split-K partials][repacked x][repacked W]. The counter
-// region is reserved whenever a workspace is used at all, so a call that only repacks never writes over the
-// counters a later split-K call on the same workspace relies on being zero.
+// Workspace layout: [4 KiB reserved][split bytes the plan reports][repacked x][repacked W]. Split K reduces inside a
+// cluster's shared memory, so plans report no split bytes and the workspace holds only operands that TMA cannot
+// read as given, repacked; the leading region stays reserved so the layout does not depend on the plan.
 constexpr size_t kCounterRegion = 4096;
 struct WsLayout {
   size_t split_bytes = 0;
@@ -227,7 +227,7 @@ int gemm_with_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, const 
     }
     if (pad_k) p.K = kp;
   }
-  // Split-K partials and counters (optional: without room for them the kernel runs one CTA per tile).
+  // Split-K bytes the plan asked for (none: split K reduces inside a cluster).
   if (ws != nullptr && L.split_bytes > 0 && workspace_bytes >= L.split_bytes) {
     p.ws_split = ws;
     p.ws_split_bytes = L.split_bytes;

@@ -8,11 +8,12 @@
 // device array of a fixed size that every GPU loading this library keeps until process exit; the entry point
 // itself calls no cudaMalloc, cudaFree or allocating library routine.
 //
-// Sharing rules: every call on a device uses the same array, and the array keeps the last call's contents. The
-// split-K tile counters at its start must be zero before a call; the kernels leave them zero, and the first call
-// on each device clears them once (so that first call must not be inside a stream capture). Calls whose work
-// overlaps on the GPU (different streams, or host threads racing on one device) race on the array: callers must
-// serialise them, e.g. by issuing every call on one stream.
+// Sharing rules: every call on a device uses the same array, and the array keeps the last call's contents (the
+// operands a call had to repack; split K reduces inside a cluster and leaves nothing there). The first call on
+// each device resolves the array's address and clears its leading 64 KiB once, synchronising its stream, so that
+// first call must not be inside a stream capture. Calls whose work overlaps on the GPU (different streams, or host
+// threads racing on one device) race on the array: callers must serialise them, e.g. by issuing every call on one
+// stream.
 #include <cstring>
 #include <mutex>
 
@@ -21,7 +22,7 @@
 
 namespace npub200 {
 
-// The shared scratch (split-K counters, f32 partials, repacked operands). Host code sees only a stand-in for this
+// The shared scratch (repacked operands, after a reserved leading region). Host code sees only a stand-in for this
 // symbol; its device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NPUB200_NOALLOC_SCRATCH_BYTES];
 
@@ -30,16 +31,15 @@ namespace {
 std::mutex g_setup_mutex;
 void* g_scratch_ptr[64] = {nullptr};
 
-// Once per device, with that device current: resolve the array's device address and clear the split-K counters.
+// Once per device, with that device current: resolve the array's device address and clear its leading region.
 int noalloc_setup(int device, cudaStream_t stream, void** out) {
   std::lock_guard<std::mutex> lock(g_setup_mutex);
   if (g_scratch_ptr[device] == nullptr) {
     void* p = nullptr;
     if (int rc = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)"))
       return rc;
-    // The counters occupy the first 4 KiB; clearing 64 KiB covers them with room to spare.
-    if (int rc = check_cuda(cudaMemsetAsync(p, 0, 65536, stream), "clear no-alloc scratch counters")) return rc;
-    if (int rc = check_cuda(cudaStreamSynchronize(stream), "clear no-alloc scratch counters (sync)")) return rc;
+    if (int rc = check_cuda(cudaMemsetAsync(p, 0, 65536, stream), "clear no-alloc scratch")) return rc;
+    if (int rc = check_cuda(cudaStreamSynchronize(stream), "clear no-alloc scratch (sync)")) return rc;
     g_scratch_ptr[device] = p;
   }
   *out = g_scratch_ptr[device];
@@ -48,12 +48,12 @@ int noalloc_setup(int device, cudaStream_t stream, void** out) {
 
 }  // namespace
 
-// After a kernel reported a failure its split-K counters may be left non-zero: clear them (no-op when the array
-// was never used on this device).
+// After a kernel reported a failure: clear the leading region again (no-op when the array was never used on this
+// device).
 int noalloc_reset_counters(int device, cudaStream_t stream) {
   std::lock_guard<std::mutex> lock(g_setup_mutex);
   if (device < 0 || device >= 64 || g_scratch_ptr[device] == nullptr) return kOk;
-  return check_cuda(cudaMemsetAsync(g_scratch_ptr[device], 0, 65536, stream), "clear no-alloc scratch counters");
+  return check_cuda(cudaMemsetAsync(g_scratch_ptr[device], 0, 65536, stream), "clear no-alloc scratch");
 }
 
 }  // namespace npub200

@@ -55,9 +55,9 @@ def release_weight(handle: int) -> None:
     _lib.call("npub200_weight_release", handle)
 
 
-# One persistent workspace per (device, stream): its leading split-K counters must be zero the first time it is
-# used and the kernels leave them zero, so it is allocated zeroed once and only ever grown (never handed back to the
-# caching allocator while this process may still launch on that stream).
+# One persistent workspace per (device, stream) for operands TMA cannot read as given (repacked copies): allocated
+# zeroed once and only ever grown, never handed back to the caching allocator while this process may still launch
+# on that stream. Split K needs none: it reduces inside a cluster's shared memory.
 _WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
 
 
@@ -71,7 +71,7 @@ def _gemm_workspace(x: torch.Tensor, w: torch.Tensor | None, M: int, K: int, N: 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
     """The zeroed per-(device, stream) workspace shared by the GEMM and convolution calls on that stream (grown to
-    a power of two, at least 4 MiB); their split-K counters are left zero by the kernels."""
+    a power of two, at least 4 MiB)."""
     if nbytes == 0:
         return None
     key = (device.index or 0, torch.cuda.current_stream(device).cuda_stream)
@@ -85,7 +85,7 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
 
 
 def reset_workspaces() -> None:
-    """Re-zero the cached workspaces (after a kernel aborted, its split-K counters may be left non-zero)."""
+    """Re-zero the cached workspaces (after a kernel aborted)."""
     for ws in _WORKSPACES.values():
         ws.zero_()
 
