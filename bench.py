@@ -216,25 +216,37 @@ class GpuWorkload:
             sum(t.numel() * t.element_size() for a in self.attn for t in a[:4])
 
     def step(self, dist, events=None):
-        """One pass. `events` (three pre-created timing events) marks the start of the GEMM launches, their end (the
-        start of the attention launches) and the end of the attention launches: only the two segment boundaries carry
-        an event, so the launches inside each segment keep their programmatic-dependent-launch overlap."""
+        """One pass. `events` (pre-created timing events, see make_events) marks the start of each M group of the
+        sweep (the sweep runs in M order), the end of the GEMM launches (the start of the attention launches) and
+        the end of the attention launches: only segment boundaries carry an event, so the launches inside a segment
+        keep their programmatic-dependent-launch overlap."""
         k = self.k
-        if events is not None:
-            events[0].record()
+        groups = self.m_groups()
+        group = -1
         for (x, w, b, out, h, _, _) in self.gemms:
+            if events is not None and groups.index(x.shape[0]) != group:
+                group = groups.index(x.shape[0])
+                events[group].record()
             k.gemm(x, w, b, out=out, handle=h)
         if events is not None:
-            events[1].record()
+            events[len(groups)].record()
         for (q, kk, v, out, full, H, _) in self.attn:
             k.attention(q, kk, v, H, out=out)
             if full is not None:
                 dist.pg.all_gather_into_tensor(full, out)
         if events is not None:
-            events[2].record()
+            events[len(groups) + 1].record()
+
+    def m_groups(self) -> list[int]:
+        seen = []
+        for g in self.gemms:
+            if g[0].shape[0] not in seen:
+                seen.append(g[0].shape[0])
+        return seen
 
     def make_events(self, external: bool = False) -> list:
-        return [torch.cuda.Event(enable_timing=True, external=external) for _ in range(3)]
+        """[start of M group 0, 1, ..., GEMM end = attention start, attention end]"""
+        return [torch.cuda.Event(enable_timing=True, external=external) for _ in range(len(self.m_groups()) + 2)]
 
     def capture(self, dist, events=None) -> torch.cuda.CUDAGraph:
         """One step captured as a CUDA graph (kernels launched back to back by the GPU, no host in the loop). The
@@ -451,8 +463,14 @@ def run_ours(args, dist) -> None:
     kernels.check_status(device)
     ms_local = t0.elapsed_time(t1) / args.steps
     ms = dist.max(ms_local, device)
-    gemm_ms = events[0].elapsed_time(events[1])
-    attn_ms = events[1].elapsed_time(events[2])
+    n_groups = len(wl.m_groups())
+    gemm_ms = events[0].elapsed_time(events[n_groups])
+    attn_ms = events[n_groups].elapsed_time(events[n_groups + 1])
+    by_m = {}
+    for gi, M in enumerate(wl.m_groups()):
+        g_ms = events[gi].elapsed_time(events[gi + 1])
+        g_fl = sum(g[5] for g in wl.gemms if g[0].shape[0] == M)
+        by_m[str(M)] = {"us": round(g_ms * 1e3, 1), "tflops": round(g_fl / (g_ms / 1e3) / 1e12, 1)}
     gflops, aflops = step_flops()
     total = (gflops + aflops) * dist.world
     value = total / (ms / 1e3) / 1e12
@@ -469,6 +487,7 @@ def run_ours(args, dist) -> None:
                 "gemm_launch_us": round(gemm_ms * 1e3 / len(wl.gemms), 3),
                 "gemm_ms_per_step": round(gemm_ms, 4),
                 "attention_ms_per_step": round(attn_ms, 4),  # with N > 1 this segment includes the all-gathers
+                "gemm_by_m": {m: dict(v, frac=round(v["tflops"] / peak, 4)) for m, v in by_m.items()},
                 "gemm_tflops": round(achieved, 1),
                 "attention_tflops": round(aflops / (attn_ms / 1e3) / 1e12, 1) if attn_ms else None,
                 "timing": "CUDA events at the GEMM and attention segment boundaries of the timed region's last step "
