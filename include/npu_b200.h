@@ -138,6 +138,19 @@ int npub200_group_norm_scratch_size(int64_t n, int64_t groups, size_t* bytes_out
 int npub200_layer_norm(const void* x, int64_t rows, int64_t cols, int64_t ldx, const void* gamma, const void* beta,
                        int param_dtype, float eps, void* out, int64_t ldo, void* stream);
 
+/* The two data-movement steps of an SD1.5 UNet decoder on NHWC (channels-last) activations, which the reference
+ * leaves to the host with the rest of the UNet (docs/02-results.md:411-413). Elements are any two-byte type (bf16,
+ * f16); channel counts and row strides are multiples of 8 elements, tensors 16-byte aligned (else
+ * NPUB200_EUNSUPPORTED); out must not overlap a source (NPUB200_EINVAL). Allocate nothing.
+ * npub200_upsample_nearest2x: nearest-neighbour 2x upsampling (torch's F.interpolate(scale_factor=2,
+ *   mode="nearest") of an Upsample block): x dense [n][h][w][c] -> out dense [n][2h][2w][c],
+ *   out[i][y][x] = x[i][y/2][x/2].
+ * npub200_concat_channels: the skip concatenation in front of each output ResBlock (torch.cat along channels):
+ *   out[p][0:ca] = a[p][:], out[p][ca:ca+cb] = b[p][:] for pixels p, rows of a/b/out lda/ldb/ldo elements apart. */
+int npub200_upsample_nearest2x(const void* x, int64_t n, int64_t h, int64_t w, int64_t c, void* out, void* stream);
+int npub200_concat_channels(const void* a, int64_t lda, int64_t ca, const void* b, int64_t ldb, int64_t cb,
+                            int64_t pixels, void* out, int64_t ldo, void* stream);
+
 /* ----------------------------------------------------------------------------------------------------------
  * GEMM without a workspace, for callers that cannot allocate device memory (a host whose device memory is owned
  * by its own pool manager and may not grow during a request, an FFI binding holding only the pointers it was

@@ -43,6 +43,9 @@ _SIGNATURES = {
     "npub200_group_norm_scratch_size": (ctypes.c_int, [_c_i64, _c_i64, ctypes.POINTER(ctypes.c_size_t)]),
     "npub200_layer_norm": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_p, ctypes.c_int, ctypes.c_float, _c_p,
                                           _c_i64, _c_p]),
+    "npub200_upsample_nearest2x": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p]),
+    "npub200_concat_channels": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64,
+                                               _c_p]),
     "npub200_gemm_residual": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p, ctypes.c_int,
                                              _c_p, _c_i64, _c_p, _c_i64, ctypes.c_int, _c_p, ctypes.c_size_t,
                                              ctypes.c_int, _c_p]),

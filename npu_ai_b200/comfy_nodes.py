@@ -149,6 +149,10 @@ class B200Runtime:
         self.pending_res: dict[int, torch.Tensor] = {}
         # LayerNorms of those blocks (norm1/norm2/norm3) on the row-wise LayerNorm kernel: id -> (f32 gamma, beta).
         self.lnorms: dict[int, tuple] = {}
+        # Upsample blocks whose nearest 2x step runs on the NHWC upsampling kernel, and spatial transformers whose
+        # closing residual add goes into proj_out's GEMM epilogue: id(module) -> (GroupNorm, proj_in, proj_out).
+        self.upsamples: set[int] = set()
+        self.stransformers: dict[int, tuple] = {}
         self.enabled = False
         self.record_only = False
         self.recorded: set[tuple[int, int, int]] = set()
@@ -261,6 +265,20 @@ class B200Runtime:
                 self.resblocks[id(mod)] = plan
                 self.installed[id(mod)] = (mod, mod.forward)
                 mod.forward = types.MethodType(_gpu_resblock_forward, mod)
+        for mod in dm.modules():
+            if id(mod) in self.installed:
+                continue
+            if (type(mod).__name__ == "Upsample" and getattr(mod, "dims", 2) == 2 and getattr(mod, "use_conv", True)
+                    and self.convs.get(id(getattr(mod, "conv", None)), ("",))[0] == "3x3"):
+                self.upsamples.add(id(mod))
+                self.installed[id(mod)] = (mod, mod.forward)
+                mod.forward = types.MethodType(_gpu_upsample_forward, mod)
+                continue
+            plan = _stransformer_plan(mod, self)
+            if plan is not None:
+                self.stransformers[id(mod)] = plan
+                self.installed[id(mod)] = (mod, mod.forward)
+                mod.forward = types.MethodType(_gpu_spatial_transformer_forward, mod)
         by_width: dict[int, list] = {}
         for mod in dm.modules():
             if id(mod) in self.resblocks and id(mod) not in self.emb_slices:
@@ -315,6 +333,8 @@ class B200Runtime:
         self.norms.clear()
         self.lnorms.clear()
         self.resblocks.clear()
+        self.upsamples.clear()
+        self.stransformers.clear()
         self.tblocks.clear()
         self.pending_res.clear()
         self.fused_groups.clear()
@@ -474,8 +494,84 @@ def _gpu_conv_forward(self, x: torch.Tensor) -> torch.Tensor:
                           memory_format=torch.channels_last)
         kernels.conv3x3(x.permute(0, 2, 3, 1), wt, bias, out=out.permute(0, 2, 3, 1))
         return out
-    y = rt.gemm.linear(x.permute(0, 2, 3, 1), wt, bias, out_dtype=torch.bfloat16)  # [n, h, w, cout]
+    res = rt.pending_res.get(id(self))
+    if res is not None and _cl_bf16(res) and tuple(res.shape) == (n, self.out_channels, h, w):
+        del rt.pending_res[id(self)]  # consumed: the residual add happens in this GEMM's epilogue
+        y = rt.gemm.linear(x.permute(0, 2, 3, 1), wt, bias, out_dtype=torch.bfloat16,
+                           residual=res.permute(0, 2, 3, 1))
+    else:
+        y = rt.gemm.linear(x.permute(0, 2, 3, 1), wt, bias, out_dtype=torch.bfloat16)  # [n, h, w, cout]
     return y.permute(0, 3, 1, 2)
+
+
+def _own_forward(rt, mod):
+    """The forward a module had before the takeover (its class's forward once the runtime is gone)."""
+    if rt is not None and id(mod) in rt.installed:
+        return rt.installed[id(mod)][1]
+    return types.MethodType(type(mod).forward, mod)
+
+
+def _gpu_upsample_forward(self, x, *args, **kwargs):
+    """Upsample.forward (nearest-neighbour 2x, then the 3x3 convolution) with the 2x step on the NHWC upsampling
+    kernel for channels-last bf16 activations. A target size other than exactly 2x (the `output_shape` a UNet passes
+    for odd encoder sizes) and every other input keep the module's own forward."""
+    rt = _RUNTIME
+    orig = _own_forward(rt, self)
+    output_shape = kwargs.get("output_shape", args[0] if args else None)
+    if (rt is None or id(self) not in rt.upsamples or not _runtime_on(rt) or not _cl_bf16(x) or x.shape[1] % 8
+            or len(args) > 1 or any(k != "output_shape" for k in kwargs)
+            or (output_shape is not None and tuple(output_shape[2:4]) != (2 * x.shape[2], 2 * x.shape[3]))):
+        return orig(x, *args, **kwargs)
+    from . import kernels
+    return self.conv(kernels.upsample_nearest2x(x))
+
+
+def _stransformer_plan(mod, rt):
+    """(GroupNorm, proj_in, proj_out) of an SD1.5-style SpatialTransformer (GroupNorm, 1x1 convolution in and out
+    around its transformer blocks, + x) whose three were taken over, or None. Linear-projection variants keep
+    their own forward."""
+    if type(mod).__name__ != "SpatialTransformer" or getattr(mod, "use_linear", False):
+        return None
+    norm, pin, pout = (getattr(mod, nm, None) for nm in ("norm", "proj_in", "proj_out"))
+    if not isinstance(getattr(mod, "transformer_blocks", None), torch.nn.ModuleList) or id(norm) not in rt.norms:
+        return None
+    if rt.convs.get(id(pin), ("",))[0] != "1x1" or rt.convs.get(id(pout), ("",))[0] != "1x1":
+        return None
+    return (norm, pin, pout)
+
+
+def _gpu_spatial_transformer_forward(self, x, *args, **kwargs):
+    """SpatialTransformer.forward: x + proj_out(blocks(proj_in(norm(x)))) over the (b, h*w, c) tokens of a
+    channels-last activation (views, no copies), with the closing residual add in proj_out's GEMM epilogue. The
+    context may be one tensor or one per block, and transformer_options gets the block index before each block,
+    as in the UNet's own forward. Inputs with ComfyUI patches or anything else keep the module's own forward."""
+    rt = _RUNTIME
+    orig = _own_forward(rt, self)
+    names = ("context", "transformer_options")
+    plan = rt.stransformers.get(id(self)) if rt is not None else None
+    bound = dict(zip(names, args))
+    bound.update(kwargs)
+    to = bound.get("transformer_options")
+    if (plan is None or not _runtime_on(rt) or len(args) > 2 or any(k not in names for k in kwargs)
+            or self.training or not _cl_bf16(x) or (to is not None and not isinstance(to, dict))
+            or (to or {}).get("patches") or (to or {}).get("patches_replace")):
+        return orig(x, *args, **kwargs)
+    norm, proj_in, proj_out = plan
+    blocks = self.transformer_blocks
+    context = bound.get("context")
+    if not isinstance(context, list):
+        context = [context] * len(blocks)
+    b, c, h, w = x.shape
+    if to is not None:
+        to["activations_shape"] = list(x.shape)
+    t = proj_in(norm(x))
+    t = t.permute(0, 2, 3, 1).reshape(b, h * w, t.shape[1])
+    for i, blk in enumerate(blocks):
+        if to is not None:
+            to["block_index"] = i
+        t = blk(t, context=context[i], transformer_options=to if to is not None else {})
+    t = t.reshape(b, h, w, t.shape[-1]).permute(0, 3, 1, 2)
+    return _with_residual(rt, proj_out, x, lambda: proj_out(t))
 
 
 def _gpu_group_norm_forward(self, x: torch.Tensor) -> torch.Tensor:

@@ -383,6 +383,15 @@ int npub200_layer_norm(const void* x, int64_t rows, int64_t cols, int64_t ldx, c
                            static_cast<cudaStream_t>(stream));
 }
 
+int npub200_upsample_nearest2x(const void* x, int64_t n, int64_t h, int64_t w, int64_t c, void* out, void* stream) {
+  return upsample_nearest2x_launch(x, n, h, w, c, out, static_cast<cudaStream_t>(stream));
+}
+
+int npub200_concat_channels(const void* a, int64_t lda, int64_t ca, const void* b, int64_t ldb, int64_t cb,
+                            int64_t pixels, void* out, int64_t ldo, void* stream) {
+  return concat_channels_launch(a, lda, ca, b, ldb, cb, pixels, out, ldo, static_cast<cudaStream_t>(stream));
+}
+
 int npub200_group_norm_scratch_size(int64_t n, int64_t groups, size_t* bytes_out) {
   if (bytes_out == nullptr) return fail(kErrInvalid, "null output pointer");
   if (n <= 0 || groups <= 0) return fail(kErrInvalid, "group_norm sizes must be positive");

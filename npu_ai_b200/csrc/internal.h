@@ -142,6 +142,12 @@ int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t g
 // in f32 (param_f32) or bf16.
 int layer_norm_launch(const void* x, int64_t rows, int64_t cols, int64_t ldx, const void* gamma, const void* beta,
                       int param_f32, float eps, void* out, int64_t ldo, cudaStream_t stream);
+// NHWC data movement (two-byte elements): nearest 2x upsampling of a dense [n][h][w][c] tensor into
+// [n][2h][2w][c], and the channel concatenation out[p] = a[p] ++ b[p] over row-strided pixels.
+int upsample_nearest2x_launch(const void* x, int64_t n, int64_t h, int64_t w, int64_t c, void* out,
+                              cudaStream_t stream);
+int concat_channels_launch(const void* a, int64_t lda, int64_t ca, const void* b, int64_t ldb, int64_t cb,
+                           int64_t pixels, void* out, int64_t ldo, cudaStream_t stream);
 // Split-K workspace bytes the convolution's fastest plan uses (0: none).
 size_t conv3x3_workspace_bytes(int64_t n, int64_t h, int64_t w, int64_t cin, int64_t cout, int variant, int sms);
 // bf16 copy of a row-strided matrix into a dense [rows, cols_pad] buffer, zero-filling the pad columns.

@@ -302,6 +302,53 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: f
     return out
 
 
+def _nhwc_2byte(t: torch.Tensor, name: str) -> None:
+    _require_cuda(t, name)
+    if t.dtype not in (torch.bfloat16, torch.float16) or t.dim() != 4:
+        raise ValueError(f"{name} must be a 4-D bf16 or f16 tensor")
+
+
+def upsample_nearest2x(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Nearest-neighbour 2x upsampling of a channels-last [n, c, h, w] tensor (torch's
+    F.interpolate(x, scale_factor=2, mode="nearest")): returns channels-last [n, c, 2h, 2w]."""
+    _nhwc_2byte(x, "x")
+    if not x.is_contiguous(memory_format=torch.channels_last):
+        raise ValueError("upsample_nearest2x takes a channels-last tensor")
+    n, c, h, w = x.shape
+    if out is None:
+        out = torch.empty((n, c, 2 * h, 2 * w), dtype=x.dtype, device=x.device, memory_format=torch.channels_last)
+    if out.shape != (n, c, 2 * h, 2 * w) or out.dtype != x.dtype or \
+            not out.is_contiguous(memory_format=torch.channels_last):
+        raise ValueError("out must be a channels-last tensor of x's dtype shaped [n, c, 2h, 2w]")
+    with torch.cuda.device(x.device):
+        _lib.call("npub200_upsample_nearest2x", ctypes.c_void_p(x.data_ptr()), n, h, w, c,
+                  ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(_stream_ptr(x.device)))
+    return out
+
+
+def concat_channels(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """torch.cat([a, b], dim=1) of two channels-last [n, c, h, w] tensors: returns the channels-last
+    [n, ca + cb, h, w] concatenation."""
+    _nhwc_2byte(a, "a")
+    _nhwc_2byte(b, "b")
+    if a.dtype != b.dtype or a.device != b.device or a.shape[0] != b.shape[0] or a.shape[2:] != b.shape[2:]:
+        raise ValueError("a and b must share dtype, device, batch and spatial size")
+    if not (a.is_contiguous(memory_format=torch.channels_last) and b.is_contiguous(memory_format=torch.channels_last)):
+        raise ValueError("concat_channels takes channels-last tensors")
+    n, ca, h, w = a.shape
+    cb = b.shape[1]
+    if out is None:
+        out = torch.empty((n, ca + cb, h, w), dtype=a.dtype, device=a.device, memory_format=torch.channels_last)
+    if out.shape != (n, ca + cb, h, w) or out.dtype != a.dtype or \
+            not out.is_contiguous(memory_format=torch.channels_last):
+        raise ValueError("out must be a channels-last tensor shaped [n, ca + cb, h, w]")
+    with torch.cuda.device(a.device):
+        _lib.call("npub200_concat_channels", ctypes.c_void_p(a.data_ptr()), ca, ca, ctypes.c_void_p(b.data_ptr()),
+                  cb, cb, n * h * w, ctypes.c_void_p(out.data_ptr()), ca + cb,
+                  ctypes.c_void_p(_stream_ptr(a.device)))
+    return out
+
+
 def _bshd_strides(t: torch.Tensor, head_major: bool) -> tuple[int, int, int]:
     """(batch, seq, head) element strides of a (B, S, H, D) view given as (B, S, H*D) or (B, H, S, D)."""
     if head_major:

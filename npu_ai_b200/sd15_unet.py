@@ -12,6 +12,9 @@ Hooks that mirror ComfyUI's, so the reference's node logic applies unchanged:
   * every Linear is a plain torch.nn.Linear (the node swaps its `forward`, comfyui node :119-136);
   * attention calls `transformer_options["optimized_attention_override"](func, q, k, v, heads, ...)` when set
     (installed by the node, comfyui node :358-359), with `func` the model's own attention (torch SDPA).
+The one place the model itself calls this package is the decoder's skip concatenation, which lives in the UNet's
+forward rather than in a module the node can take over: channels-last bf16/f16 CUDA activations are concatenated
+by the NHWC concatenation kernel, everything else (CPU runs, f32) by torch.cat.
 """
 from __future__ import annotations
 
@@ -144,6 +147,16 @@ class Upsample(nn.Module):
         return self.conv(F.interpolate(x, scale_factor=2.0, mode="nearest"))
 
 
+def cat_channels(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """torch.cat([a, b], dim=1) of the decoder activation and its skip tensor."""
+    if (a.is_cuda and a.dim() == 4 and a.dtype in (torch.bfloat16, torch.float16) and b.dtype == a.dtype
+            and a.shape[1] % 8 == 0 and b.shape[1] % 8 == 0 and a.is_contiguous(memory_format=torch.channels_last)
+            and b.is_contiguous(memory_format=torch.channels_last)):
+        from . import kernels
+        return kernels.concat_channels(a, b)
+    return torch.cat([a, b], dim=1)
+
+
 def timestep_embedding(t: torch.Tensor, dim: int, max_period: float = 10000.0) -> torch.Tensor:
     half = dim // 2
     freqs = torch.exp(-math.log(max_period) * torch.arange(half, dtype=torch.float32, device=t.device) / half)
@@ -208,7 +221,7 @@ class SD15UNet(nn.Module):
             hs.append(h)
         h = self._run(self.middle_block, h, emb, context, transformer_options)
         for blk in self.output_blocks:
-            h = torch.cat([h, hs.pop()], dim=1)
+            h = cat_channels(h, hs.pop())
             h = self._run(blk, h, emb, context, transformer_options)
         return self.out(h)
 

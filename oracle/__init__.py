@@ -13,6 +13,8 @@ checks its NPU results against.
   * 3x3 convolution: `F.conv2d` in f32 on bf16-rounded operands, bias then residual added in f32 (the host-side
     convolutions of the UNet around the offloaded layers, docs/02-results.md:411-413).
   * GroupNorm (+ SiLU): `F.group_norm` in f32 on bf16-rounded activations (the same host-side work).
+  * Nearest 2x upsampling and the skip concatenation of the UNet decoder: `F.interpolate` and `torch.cat`, pure
+    copies (the same host-side work).
   * GEGLU feed-forward projection: the projection as above, then value * gelu(gate) in f32 with the exact (erf)
     GELU, as the host side of a transformer block computes it after the reference's Linear offload
     (docs/02-results.md:411-413 lists GEGLU among the host work; ComfyUI's GEGLU module is
@@ -22,5 +24,6 @@ Pinning: tests/golden/ holds fixtures produced by running the reference's CPU fa
 accuracy figures (docs/02-results.md:709) that the attention oracle reproduces on the reference's own seeded
 inputs; see tests/test_oracle.py.
 """
-from .reference_ops import (attention_ref, bf16_round, conv3x3_ref, cosine, geglu_ref,  # noqa: F401
-                            group_norm_ref, layer_norm_ref, linear_ref, rel_l2_err, rel_max_err)
+from .reference_ops import (attention_ref, bf16_round, concat_channels_ref, conv3x3_ref, cosine,  # noqa: F401
+                            geglu_ref, group_norm_ref, layer_norm_ref, linear_ref, rel_l2_err, rel_max_err,
+                            upsample_nearest2x_ref)

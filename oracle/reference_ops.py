@@ -68,6 +68,17 @@ def layer_norm_ref(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps
     return F.layer_norm(x, (x.shape[-1],), gamma.detach().to("cpu").float(), beta.detach().to("cpu").float(), eps)
 
 
+def upsample_nearest2x_ref(x_nchw: torch.Tensor) -> torch.Tensor:
+    """Nearest-neighbour 2x upsampling of an [n, c, h, w] tensor, as the UNet's Upsample block computes it on the
+    host (F.interpolate(scale_factor=2, mode="nearest")): a pure copy, so any layout and dtype is exact."""
+    return F.interpolate(x_nchw, scale_factor=2.0, mode="nearest")
+
+
+def concat_channels_ref(a_nchw: torch.Tensor, b_nchw: torch.Tensor) -> torch.Tensor:
+    """The decoder's skip concatenation of two [n, c, h, w] tensors along channels (torch.cat on the host)."""
+    return torch.cat([a_nchw, b_nchw], dim=1)
+
+
 def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
                   head_major: bool = False) -> torch.Tensor:
     """f32 softmax(bf16(q) bf16(k)^T * scale) bf16(v) for every (batch, head) pair.

@@ -201,6 +201,9 @@ def test_unet_channels_last_on_conv_kernels(cuda_device):
         # all 22 time-embedding projections in one grouped GEMM per UNet call
         assert len(rt.emb_slices) == 22 and len(rt.emb_groups) == 1, (len(rt.emb_slices), len(rt.emb_groups))
         assert len(rt.emb_cache) == 1
+        assert len(rt.upsamples) == 3, len(rt.upsamples)             # decoder 2x steps on the NHWC kernel
+        assert len(rt.stransformers) == 16, len(rt.stransformers)    # residual add in proj_out's epilogue
+        assert not rt.pending_res                                     # every offered residual was consumed
         assert torch.isfinite(y).all()
         assert rel_l2_err(y, ref) < 3e-2, rel_l2_err(y, ref)
     finally:
