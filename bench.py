@@ -545,6 +545,51 @@ def run_e2e(args, dist, device, total_flops) -> dict:
 # ----------------------------------------------------------------------------------------------------------------
 # UNet workload: SD1.5-architecture UNet denoise steps (batch 2 with 4 Euler steps; batch 16, sharded over GPUs)
 # ----------------------------------------------------------------------------------------------------------------
+def _kernel_kind(name: str) -> str:
+    if "attention_fwd" in name:
+        return "attention"
+    if "gemm_bf16_tcgen05" in name:
+        mode = name.split("gemm_bf16_tcgen05_kernel<", 1)[-1].split(",")
+        return {"1": "GEGLU GEMM", "2": "3x3 convolution"}.get(mode[2].strip() if len(mode) > 2 else "", "GEMM")
+    for key, kind in (("gn_", "GroupNorm"), ("layer_norm", "LayerNorm"), ("concat_channels", "NHWC copy"),
+                      ("upsample_nearest2x", "NHWC copy"), ("repack_rows", "GEMM operand repack")):
+        if key in name:
+            return kind
+    if "conv" in name or "cutlass" in name:
+        return "torch convolution (cuDNN)"
+    if "nvjet" in name or "gemm" in name.lower():
+        return "torch GEMM (cuBLAS)"
+    return "torch elementwise / copies"
+
+
+def kernel_times(replay, steps: int = 3) -> str:
+    """Device time of one replay per kernel kind (torch profiler over `steps` replays). Kernels launched with
+    programmatic dependent launch start early and wait, so their own durations overlap; each kernel is charged the
+    part of the replay's busy span it adds past the ends of the kernels before it."""
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            replay()
+        torch.cuda.synchronize()
+    evs = sorted((e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA
+                  and e.time_range.end > e.time_range.start), key=lambda e: e.time_range.start)
+    charged: dict[str, list] = {}
+    frontier = None
+    for e in evs:
+        s0, s1 = e.time_range.start, e.time_range.end
+        add = (s1 - s0) if frontier is None or s0 >= frontier else max(0.0, s1 - frontier)
+        frontier = s1 if frontier is None else max(frontier, s1)
+        c = charged.setdefault(_kernel_kind(e.name), [0, 0.0])
+        c[0] += 1
+        c[1] += add
+    total = sum(t for _, t in charged.values())
+    lines = [f"{'kernel kind':28s} {'launches':>9s} {'us/step':>9s} {'share':>6s}"]
+    for kind, (n, t) in sorted(charged.items(), key=lambda kv: -kv[1][1]):
+        lines.append(f"{kind:28s} {n / steps:9.1f} {t / steps:9.1f} {100 * t / total:5.1f}%")
+    lines.append(f"{'busy span':28s} {len(evs) / steps:9.1f} {total / steps:9.1f}")
+    return "\n".join(lines)
+
+
 def run_unet(args, dist) -> None:
     """Euler CFG denoise steps of a random-init SD1.5-architecture UNet with every Linear and attention on the B200
     kernels (through the ComfyUI node runtime). The batch (prompts x CFG pair) is sharded over the ranks with each
@@ -630,6 +675,8 @@ def run_unet(args, dist) -> None:
         dist.barrier()
         clocks = sampler.stop() if sampler is not None else None
         kernels.check_status(device)
+        if args.kernel_times and dist.world == 1:
+            print(kernel_times(g.replay), file=sys.stderr, flush=True)
     ms = dist.max(t0.elapsed_time(t1) / args.steps, device)
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
@@ -706,9 +753,24 @@ def run_case(args) -> None:
         # bytes: one read and one write of the tensor
         fn, flops = (lambda: kernels.layer_norm(x, g, bb, out=out)), 0.0
         gn_bytes = 2.0 * x.numel() * 2
+    elif kind == "up":
+        n, c, h, w_ = d
+        x = _seeded((n, c, h, w_), 1.0, 1, device).contiguous(memory_format=torch.channels_last)
+        out = torch.empty((n, c, 2 * h, 2 * w_), dtype=torch.bfloat16, device=device, memory_format=torch.channels_last)
+        # bytes: one read of the input, one write of the 4x output
+        fn, flops = (lambda: kernels.upsample_nearest2x(x, out=out)), 0.0
+        gn_bytes = 5.0 * x.numel() * 2
+    elif kind == "cat":
+        n, ca, cb, h, w_ = d
+        a = _seeded((n, ca, h, w_), 1.0, 1, device).contiguous(memory_format=torch.channels_last)
+        b = _seeded((n, cb, h, w_), 1.0, 2, device).contiguous(memory_format=torch.channels_last)
+        out = torch.empty((n, ca + cb, h, w_), dtype=torch.bfloat16, device=device, memory_format=torch.channels_last)
+        # bytes: one read of both sources, one write of the output
+        fn, flops = (lambda: kernels.concat_channels(a, b, out=out)), 0.0
+        gn_bytes = 2.0 * out.numel() * 2
     else:
         raise SystemExit(f"unknown case kind {kind!r} (gemm:M,K,N, attn:B,H,Sq,Skv,D, geglu:M,K,n, "
-                         "conv:n,h,w,cin,cout, gn:n,h,w,c or ln:rows,c)")
+                         "conv:n,h,w,cin,cout, gn:n,h,w,c, ln:rows,c, up:n,c,h,w or cat:n,ca,cb,h,w)")
     for _ in range(args.warmup):
         fn()
     torch.cuda.synchronize()
@@ -722,7 +784,7 @@ def run_case(args) -> None:
     ms = e0.elapsed_time(e1) / args.steps
     print(json.dumps({"case": args.case, "us_per_launch": round(ms * 1e3, 2),
                       "tflops": round(flops / ms / 1e9, 1),
-                      **({"gbs": round(gn_bytes / ms / 1e6, 1)} if kind in ("gn", "ln") else {})}), flush=True)
+                      **({"gbs": round(gn_bytes / ms / 1e6, 1)} if gn_bytes else {})}), flush=True)
 
 
 def main(argv=None) -> int:
@@ -734,12 +796,16 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--case", default=None, help="time one kernel: gemm:M,K,N, attn:B,H,Sq,Skv,D, geglu:M,K,n, "
-                                                   "conv:n,h,w,cin,cout, gn:n,h,w,c or ln:rows,c")
+                                                   "conv:n,h,w,cin,cout, gn:n,h,w,c, ln:rows,c, up:n,c,h,w or "
+                                                   "cat:n,ca,cb,h,w")
     ap.add_argument("--workload", choices=["hotpath", "unet"], default="hotpath",
                     help="hotpath: the GEMM sweep + attention blocks (default); unet: SD1.5 UNet denoise steps")
     ap.add_argument("--batch", type=int, default=2, help="unet: images per step, both CFG halves (2 = 1 prompt)")
     ap.add_argument("--latent", type=int, default=64, help="unet: latent height/width")
     ap.add_argument("--unet-steps", type=int, default=4, help="unet: Euler steps per image")
+    ap.add_argument("--kernel-times", action="store_true",
+                    help="unet: after the timed region, print the step's device time per kernel kind to stderr "
+                         "(torch profiler over three extra graph replays; the JSON line is unaffected)")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     if args.case:

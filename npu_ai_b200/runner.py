@@ -135,6 +135,8 @@ class NpuGemm:
         around each call so `stats["npu_seconds"]` holds GPU time (resolved lazily, no per-call sync)."""
         t0 = time.perf_counter()
         if device is None:
+            if not torch.cuda.is_available():
+                raise RuntimeError("NpuGemm needs a CUDA device and none is available; there is no CPU path")
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
         if self.device.type != "cuda":

@@ -204,6 +204,7 @@ def test_unet_channels_last_on_conv_kernels(cuda_device):
         assert len(rt.upsamples) == 3, len(rt.upsamples)             # decoder 2x steps on the NHWC kernel
         assert len(rt.stransformers) == 16, len(rt.stransformers)    # residual add in proj_out's epilogue
         assert not rt.pending_res                                     # every offered residual was consumed
+        assert id(model.out) in rt.norm_silu                          # output head: SiLU inside the GroupNorm
         assert torch.isfinite(y).all()
         assert rel_l2_err(y, ref) < 3e-2, rel_l2_err(y, ref)
     finally:
