@@ -191,7 +191,9 @@ int npub200_status_read(void* stream, uint32_t* bits_out, int clear);
 
 /* Test hooks (failure detection without a GPU fault): per-wait deadline in ns (0 restores the default), and
  * debug flags applied to the next launches (bit 0: the MMA role waits on a barrier nothing signals, so the
- * bounded wait expires and the kernel takes its abort path). */
+ * bounded wait expires and the kernel takes its abort path; bits 1, 2: npub200_group_norm uses its two-launch or
+ * its one-launch cooperative form, the latter where it takes the shape, so tests cover both forms on the same
+ * inputs). */
 int npub200_set_wait_timeout_ns(uint64_t ns);
 int npub200_set_debug_flags(uint32_t flags);
 

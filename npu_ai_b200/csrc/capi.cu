@@ -372,7 +372,7 @@ int npub200_conv3x3(const void* x, int64_t n, int64_t h, int64_t w, int64_t cin,
 int npub200_group_norm(const void* x, int64_t n, int64_t hw, int64_t c, int64_t groups, const float* gamma,
                        const float* beta, float eps, int apply_silu, void* out, float* stats, void* stream) {
   return group_norm_launch(x, n, hw, c, groups, gamma, beta, eps, apply_silu, out, stats,
-                           static_cast<cudaStream_t>(stream));
+                           static_cast<cudaStream_t>(stream), g_debug_flags.load());
 }
 
 int npub200_layer_norm(const void* x, int64_t rows, int64_t cols, int64_t ldx, const void* gamma, const void* beta,

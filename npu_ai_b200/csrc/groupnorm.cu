@@ -3,8 +3,8 @@
 // GroupNorm/LayerNorm, ..."); on B200 it matters because the convolutions run channels-last: torch's GroupNorm
 // converts such tensors to NCHW and back, which costs more than the normalisation itself.
 //
-// One launch normally (gn_fused_kernel, a cooperative grid: every block resident), two as a fallback; both
-// HBM-bound and deterministic (fixed-order reductions):
+// One launch normally (gn_fused_kernel, a cooperative grid: every block resident), two for small tensors and as a
+// fallback; both HBM-bound and deterministic (fixed-order reductions):
 //   gn_fused_kernel  blocks over (pixel slice, image) read their pixels as whole 16-byte channel chunks, sum per
 //                    channel in f32, fold channels into groups and publish per-slice partials; a grid barrier;
 //                    then each block combines its image's partials in slice order into (mean, rstd) and
@@ -331,7 +331,8 @@ size_t group_norm_scratch_bytes(int64_t n, int64_t groups) {
 }
 
 int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t groups, const float* gamma,
-                      const float* beta, float eps, int apply_silu, void* out, float* stats, cudaStream_t stream) {
+                      const float* beta, float eps, int apply_silu, void* out, float* stats, cudaStream_t stream,
+                      uint32_t debug) {
   const DeviceInfo* dev = nullptr;
   if (int rc = current_device_info(&dev)) return rc;
   if (x == nullptr || out == nullptr || gamma == nullptr || beta == nullptr || stats == nullptr)
@@ -351,7 +352,8 @@ int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t g
   // One launch for large tensors when every block of a grid with at least one slice per image can be resident at
   // once. Below ~4M values the grid barrier costs more than the second launch it saves (measured on the SD1.5
   // ResBlocks: batch 2 slower by ~3.6 us per call, batch 16 at 64x64 faster, 32 vs 47 us).
-  if (c <= 4096 && n * hw * c >= (int64_t(1) << 22)) {
+  const uint32_t forced = debug & (kDebugGnTwoLaunch | kDebugGnCooperative);
+  if (c <= 4096 && (forced ? forced == kDebugGnCooperative : n * hw * c >= (int64_t(1) << 22))) {
     static int per_sm[64] = {0};
     const size_t smem = fused_smem_bytes(c, groups);
     if (dev->device < 0 || dev->device >= 64) return fail(kErrInvalid, "device ordinal out of range");
@@ -388,8 +390,8 @@ int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t g
           "group_norm launch");
     }
   }
-  // Pixel slices per (image, group): enough blocks to fill the GPU, each with at least a few thousand values.
   const int64_t cg = c / groups;
+  // Pixel slices per (image, group): enough blocks to fill the GPU, each with at least a few thousand values.
   int64_t slices = std::max<int64_t>(1, (int64_t(dev->sms) * 4 + n * groups - 1) / (n * groups));
   slices = std::min<int64_t>({slices, int64_t(kGnMaxSlices), std::max<int64_t>(1, hw * cg / 4096)});
   if (int rc = check_cuda(launch_pdl(gn_stats_kernel, dim3(unsigned(groups), unsigned(n), unsigned(slices)),

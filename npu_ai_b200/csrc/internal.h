@@ -136,8 +136,12 @@ int conv3x3_launch(const ConvProblem& p, cudaStream_t stream);
 // GroupNorm (+ SiLU) over NHWC bf16: x, out [n][hw][c]; gamma, beta f32 [c]; stats: group_norm_scratch_bytes()
 // of scratch whose counters (the last n*groups words) are zero on first use and left zero.
 size_t group_norm_scratch_bytes(int64_t n, int64_t groups);
+// Debug bits 1 and 2 force the two-launch or the cooperative GroupNorm form (the latter where it applies), so tests
+// run both forms on the same shapes.
+constexpr uint32_t kDebugGnTwoLaunch = 2u, kDebugGnCooperative = 4u;
 int group_norm_launch(const void* x, int64_t n, int64_t hw, int64_t c, int64_t groups, const float* gamma,
-                      const float* beta, float eps, int apply_silu, void* out, float* stats, cudaStream_t stream);
+                      const float* beta, float eps, int apply_silu, void* out, float* stats, cudaStream_t stream,
+                      uint32_t debug);
 // LayerNorm over the last dimension of bf16 rows: x [rows][ldx], out [rows][ldo] (cols valid); gamma, beta [cols]
 // in f32 (param_f32) or bf16.
 int layer_norm_launch(const void* x, int64_t rows, int64_t cols, int64_t ldx, const void* gamma, const void* beta,
