@@ -156,6 +156,8 @@ class B200Runtime:
         # GroupNorm -> SiLU -> convolution sequences (the UNet's output head, ResBlock layer stacks) with the SiLU
         # in the GroupNorm kernel: id(Sequential) -> (GroupNorm, convolution).
         self.norm_silu: dict[int, tuple] = {}
+        # A second stream per device for work off a ResBlock's critical path (its 1x1 skip convolution).
+        self.side_streams: dict[int, torch.cuda.Stream] = {}
         self.enabled = False
         self.record_only = False
         self.recorded: set[tuple[int, int, int]] = set()
@@ -323,6 +325,14 @@ class B200Runtime:
             self.fused_member[id(m)] = id(group[0])
             col += m.out_features
         self.fused_groups[id(group[0])] = (nw, bias, members, group[0].out_features)
+
+    def side_stream(self, device: torch.device) -> torch.cuda.Stream:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        st = self.side_streams.get(idx)
+        if st is None:
+            st = torch.cuda.Stream(device=torch.device("cuda", idx))
+            self.side_streams[idx] = st
+        return st
 
     def release(self) -> None:
         for mod, orig in self.installed.values():
@@ -678,10 +688,18 @@ def _resblock_emb_rows(rt, block, emb, conv1) -> torch.Tensor:
     return cached[2][:, off:off + cout]
 
 
+# Largest ResBlock activation (pixels over the batch) whose skip convolution runs on the side stream: 8192 pixels are
+# 64 convolution row tiles, well under one wave of tiles on 148 SMs (batch 2 at the 64x64 latent's top level).
+_SIDE_STREAM_MAX_PIXELS = 8192
+
+
 def _gpu_resblock_forward(self, x, emb, *args, **kwargs):
     """ResBlock.forward in four launches plus the small time-embedding Linear: GroupNorm+SiLU, conv1 with the
     bias row of each image = conv bias + emb_layers(emb), GroupNorm+SiLU, conv2 with the skip path (x or its 1x1
-    convolution) added in the epilogue."""
+    convolution) added in the epilogue. For small activations (at most 8192 pixels, where the convolutions' grids
+    do not fill the GPU) a 1x1 skip convolution runs on a second stream, forked before the first GroupNorm and
+    joined before conv2, so it overlaps the latency-bound main chain (a parallel branch in a captured graph);
+    larger ones keep it in line, where it would only contend with a main chain that already fills the GPU."""
     rt = _RUNTIME
     plan = rt.resblocks.get(id(self)) if rt is not None else None
     if plan is None or not _runtime_on(rt) or not _cl_bf16(x) or self.training or args or \
@@ -692,6 +710,17 @@ def _gpu_resblock_forward(self, x, emb, *args, **kwargs):
     gn1, conv1, gn2, conv2, skip = plan
     n, c, h, w = x.shape
     xh = x.permute(0, 2, 3, 1)
+    main = side = None
+    if not isinstance(skip, torch.nn.Identity):
+        _kind, ws, bs = rt.convs[id(skip)]
+        if n * h * w <= _SIDE_STREAM_MAX_PIXELS:
+            main = torch.cuda.current_stream(x.device)
+            side = rt.side_stream(x.device)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                res = rt.gemm.linear(xh, ws, bs, out_dtype=torch.bfloat16)
+        else:
+            res = rt.gemm.linear(xh, ws, bs, out_dtype=torch.bfloat16)
     t1 = torch.empty_like(xh)
     g1 = rt.norms[id(gn1)]
     kernels.group_norm(xh, gn1.num_groups, g1[0], g1[1], eps=gn1.eps, silu=True, out=t1)
@@ -703,9 +732,9 @@ def _gpu_resblock_forward(self, x, emb, *args, **kwargs):
     kernels.group_norm(h1, gn2.num_groups, g2[0], g2[1], eps=gn2.eps, silu=True, out=h1)
     if isinstance(skip, torch.nn.Identity):
         res = xh
-    else:
-        _kind, ws, bs = rt.convs[id(skip)]
-        res = rt.gemm.linear(xh, ws, bs, out_dtype=torch.bfloat16)
+    elif side is not None:
+        main.wait_stream(side)
+        res.record_stream(main)  # allocated on the side stream, read and released on this one
     out = torch.empty((n, conv2.out_channels, h, w), dtype=torch.bfloat16, device=x.device,
                       memory_format=torch.channels_last)
     kernels.conv3x3(h1, rt.convs[id(conv2)][1], rt.convs[id(conv2)][2], residual=res, out=out.permute(0, 2, 3, 1))
