@@ -3,8 +3,9 @@
 Covers what the reference's node file defines (comfyui/custom_nodes/comfyui_xdna1_npu/__init__.py): the node
 classes under the reference's names (:400-409), their ComfyUI interface (INPUT_TYPES / RETURN_TYPES / FUNCTION,
 :260-291, :362-391), the attention gate's static routing rules (:39-99: masked and GQA calls, small shapes, mode
-off -> the model's own attention), and that the runner refuses to run without a CUDA device instead of falling back
-to the CPU (the reference never falls back silently either, node :5-7)."""
+off -> the model's own attention), and that the runner and every kernel wrapper refuse host tensors or a host
+without a CUDA device instead of falling back to the CPU (the reference never falls back silently either,
+node :5-7)."""
 import pytest
 import torch
 
@@ -95,3 +96,27 @@ def test_bench_kernel_kinds():
     assert bench._kernel_kind("npub200::(anonymous namespace)::concat_channels_kernel(uint4 const*)") == "NHWC copy"
     assert bench._kernel_kind("cutlass3x_sm100_tensorop_s256x128x16implicit_gemm_fprop_bf16") == \
         "torch convolution (cuDNN)"
+
+
+def _cpu_bf16(*shape):
+    return torch.zeros(*shape, dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize("call", [
+    lambda k: k.gemm(_cpu_bf16(4, 8), _cpu_bf16(16, 8)),
+    lambda k: k.gemm_geglu(_cpu_bf16(4, 8), _cpu_bf16(16, 8)),
+    lambda k: k.conv3x3(_cpu_bf16(1, 4, 4, 64), _cpu_bf16(8, 3, 3, 64)),
+    lambda k: k.group_norm(_cpu_bf16(1, 4, 4, 64), 32, torch.ones(64), torch.zeros(64)),
+    lambda k: k.layer_norm(_cpu_bf16(4, 64), torch.ones(64), torch.zeros(64)),
+    lambda k: k.upsample_nearest2x(_cpu_bf16(1, 8, 2, 2).contiguous(memory_format=torch.channels_last)),
+    lambda k: k.concat_channels(_cpu_bf16(1, 8, 2, 2), _cpu_bf16(1, 8, 2, 2)),
+    lambda k: k.attention(_cpu_bf16(1, 16, 80), _cpu_bf16(1, 16, 80), _cpu_bf16(1, 16, 80), 2),
+    lambda k: k.register_weight(_cpu_bf16(16, 8)),
+], ids=["gemm", "gemm_geglu", "conv3x3", "group_norm", "layer_norm", "upsample", "concat", "attention",
+        "register_weight"])
+def test_every_kernel_refuses_host_tensors(call):
+    """No op computes on the CPU: host tensors are refused before anything launches (the product path has no
+    fallback; callers copy to the device, as NpuGemm does for the reference's CPU inputs)."""
+    from npu_ai_b200 import kernels
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        call(kernels)
