@@ -21,6 +21,12 @@ Reported beside the device-timed value: the same metric end to end through the p
 host buffers, host<->device copies inside the timed region), the dominant kernel's roofline, the host CPU path
 (the reference's CPU fallback: F.linear / SDPA in f32 on bf16-rounded inputs) on a bounded sample, and the SM
 clocks sampled during the timed region. `--impl reference` times that CPU path alone, with all host threads.
+
+Other workloads (not the driver's line):
+  --workload unet [--batch B --latent L [--kernel-times]]  SD1.5-architecture UNet CFG denoise steps/s, batch sharded
+      over the ranks; --kernel-times prints the step's device time per kernel kind to stderr.
+  --case KIND:dims  one kernel on one shape (gemm, attn, geglu, conv, gn, ln, up, cat), the small cases the ncu
+      summaries use.
 """
 from __future__ import annotations
 
