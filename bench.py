@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark of the npu-ai offload hot path on B200: bf16 GEMM + fused attention TFLOP/s.
+"""Benchmark of the npu-ai offload hot path on B200: bf16 GEMM + fused attention TFLOP/s, and SD1.5 UNet steps/s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
@@ -7,24 +7,34 @@
 
 One step = one pass of the hot path over the SD1.5 workload the reference quotes its GEMM and attention numbers
 on (synthetic, seeded inputs of those shapes and distributions; the reference publishes no dataset for it):
-  * the shape-agnostic GEMM sweep: M in {77, 154, 256, 1024, 4096, 8192} x 11 SD1.5 (K, N) Linear shapes,
-    x ~ N(0,1), W ~ N(0, 0.02^2), b ~ N(0, 0.01^2), bf16 operands, f32 accumulation, bf16 out (66 launches);
   * the fused attention blocks: self-attention (2, 8, 4096, 4096, 40), (2, 8, 1024, 1024, 80),
     (2, 8, 256, 256, 160) and cross-attention (2, 8, 4096, 77, 40) as (B, H, Sq, Skv, d), q/k/v ~ N(0,1),
-    scale d^-0.5, all batch x head pairs in one launch each (4 launches).
+    scale d^-0.5, all batch x head pairs in one launch each (4 launches);
+  * the shape-agnostic GEMM sweep: M in {77, 154, 256, 1024, 4096, 8192} x 11 SD1.5 (K, N) Linear shapes,
+    x ~ N(0,1), W ~ N(0, 0.02^2), b ~ N(0, 0.01^2), bf16 operands, f32 accumulation, bf16 out (66 launches).
 Metric: total algorithmic FLOPs (2MKN per GEMM, 4 B H Sq Skv d per attention block, the reference's own counts)
 per second, whole job. Multi-GPU (torchrun, one rank per GPU): weak scaling. The GEMMs do not shard (a single
 Linear is microseconds; every rank runs its own replica of the sweep); the attention blocks shard over batch x
-head pairs: rank r owns batches [2r, 2r+2) of a (2N, ...) block and the outputs are all-gathered over NCCL.
+head pairs: rank r owns batches [2r, 2r+2) of a (2N, ...) block and the outputs are all-gathered over NCCL on a
+communication stream while the GEMM sweep runs.
 
-Reported beside the device-timed value: the same metric end to end through the public API (NpuGemm with pinned
-host buffers, host<->device copies inside the timed region), the dominant kernel's roofline, the host CPU path
-(the reference's CPU fallback: F.linear / SDPA in f32 on bf16-rounded inputs) on a bounded sample, and the SM
-clocks sampled during the timed region. `--impl reference` times that CPU path alone, with all host threads.
+Reported in the same JSON line:
+  * roofline: the dominant kernel (GEMM) against the measured burst bf16 peak, per sweep M group, config 1
+    (4096x320x320 with bias, bf16 out) as a standalone launch sequence over rotating buffers larger than L2
+    against its HBM roofline, and every attention block with its exponential-unit floor;
+  * e2e: the same step end to end through the public API (NpuGemm with pinned host buffers, host<->device copies
+    of inputs, biases and results inside the timed region);
+  * unet: SD1.5-architecture UNet (random init) Euler CFG denoise steps at batch 16 (8 prompts x CFG) on 64x64
+    and 128x128 latents, the batch sharded over the N ranks with latents all-gathered every step; at N = 1 also
+    batch 2 (one prompt, 4 Euler steps per image) and the host CPU's batch-2 UNet call;
+  * cpu_baseline: the reference's CPU fallback (F.linear / SDPA in f32 on bf16-rounded inputs) on a bounded
+    sample of the step, on the host cores;
+  * clocks: nvidia-smi samples over a soak of step replays directly before and through the timed region.
+`--impl reference` times that CPU path alone on the whole 70-op step, with all host threads.
 
-Other workloads (not the driver's line):
-  --workload unet [--batch B --latent L [--kernel-times]]  SD1.5-architecture UNet CFG denoise steps/s, batch sharded
-      over the ranks; --kernel-times prints the step's device time per kernel kind to stderr.
+Other modes (not the driver's line):
+  --workload unet [--batch B --latent L [--kernel-times]]  only the UNet leg, on one configuration; --kernel-times
+      prints the step's device time per kernel kind to stderr.
   --case KIND:dims  one kernel on one shape (gemm, attn, geglu, conv, gn, ln, up, cat), the small cases the ncu
       summaries use.
 """
@@ -46,11 +56,19 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "bf16 GEMM & fused-attn TFLOP/s"
+WORKLOAD = "sd15-linear-sweep+attention-blocks"
 SD15_M = [77, 154, 256, 1024, 4096, 8192]
 SD15_KN = [(320, 320), (320, 2560), (1280, 320), (768, 320), (640, 640), (640, 5120), (2560, 640), (1280, 1280),
            (1280, 10240), (5120, 1280), (768, 1280)]
 ATTN_BLOCKS = [(2, 8, 4096, 4096, 40), (2, 8, 1024, 1024, 80), (2, 8, 256, 256, 160), (2, 8, 4096, 77, 40)]
+CONFIG1 = (4096, 320, 320)  # single SD1.5 to_q Linear at the 64x64 latent
 L2_BYTES = 126 * 2**20
+SMS = 148
+EX2_PER_CLK_PER_SM = 16  # MUFU exponentials per clock per SM (measured with a probe kernel)
+
+# DRAM traffic per launch of the dominant kernel (GEMM, mean over the 66 sweep launches of one step) from the ncu
+# capture summarised in profiles/gemm_sweep_dram.md; null when that capture predates the current GEMM kernel.
+GEMM_DRAM_BYTES_PER_LAUNCH = 14401380
 
 
 def _peaks() -> dict:
@@ -58,14 +76,23 @@ def _peaks() -> dict:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
         return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
-                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "source": "measured"}
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "sm_max_mhz": float(p.get("sm_max_mhz", 1965.0)), "source": "measured"}
     except (OSError, KeyError, ValueError):
-        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0,
+                "source": "fallback"}
 
 
-# DRAM traffic per launch of the dominant kernel (GEMM, averaged over the 66 sweep launches) from the committed
-# ncu capture summarised in profiles/gemm_sweep_dram.md (mean over the 66 launches of one step).
-GEMM_DRAM_BYTES_PER_LAUNCH = 14401380
+def hotpath_config(world: int) -> dict:
+    """The `config` of the hot-path line; the reference arm prints the same object."""
+    step_bytes = sum(2 * (M * K + N * K + N + M * N) for M, K, N in gemm_shapes()) + \
+        sum(2 * B * H * D * (2 * Sq + 2 * Skv) for B, H, Sq, Skv, D in ATTN_BLOCKS)
+    return {"workload": WORKLOAD,
+            "gemm_shapes": "M{77,154,256,1024,4096,8192} x 11 SD1.5 (K,N), bf16 out, bias",
+            "attention_blocks": ATTN_BLOCKS, "per_rank_attention_batch": 2,
+            "parallelism": f"replicas(gemm)+pairs-sharded(attention) x{world}",
+            "l2": f"inputs larger than L2: {step_bytes / 2**20:.0f} MiB touched once per step vs "
+                  f"{L2_BYTES / 2**20:.0f} MiB L2"}
 
 
 # ----------------------------------------------------------------------------------------------------------------
@@ -107,14 +134,14 @@ class Dist:
 # clocks
 # ----------------------------------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples every 200 ms while the timed region runs."""
+    """nvidia-smi clock / power / throttle-reason samples every 200 ms; windows are marked on the host clock."""
     FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, uuids: list[str]):
         self.uuids = [u.lower() for u in uuids]
-        self.samples: list[list[str]] = []
+        self.samples: list[list] = []
         self.proc = None
         self.thread = None
 
@@ -134,16 +161,9 @@ class ClockSampler:
         self.thread = threading.Thread(target=reader, daemon=True)
         self.thread.start()
 
-    def mark(self, begin: bool) -> None:
-        """Bracket the timed region: only samples taken between the marks are reported."""
-        if begin:
-            self.t_begin = time.perf_counter()
-        else:
-            self.t_end = time.perf_counter()
-
-    def stop(self) -> dict:
+    def stop(self) -> None:
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -151,16 +171,23 @@ class ClockSampler:
             self.proc.kill()
         if self.thread is not None:
             self.thread.join(timeout=2)
+
+    def summary(self, t_begin: float, t_end: float, window: str) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         want = {u.lower().replace("gpu-", "") for u in self.uuids if u}
-        t_b, t_e = getattr(self, "t_begin", 0.0), getattr(self, "t_end", float("inf"))
-        timed = [s for s in self.samples if t_b <= s[8] <= t_e + 0.2] or self.samples
+        timed = [s for s in self.samples if t_begin <= s[8] <= t_end + 0.2]
         mine = [s for s in timed if s[0].lower().replace("gpu-", "") in want] or timed
-        sm = [float(s[1]) for s in mine if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in mine if s[2].replace(".", "").isdigit()]
+        num = lambda v: v.replace(".", "", 1).isdigit()  # noqa: E731
+        sm = [float(s[1]) for s in mine if num(s[1])]
+        mx = [float(s[2]) for s in mine if num(s[2])]
+        pw = [float(s[3]) for s in mine if num(s[3])]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for s in mine for i in range(4) if s[4 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(mine)}
+                "reasons": reasons, "samples": len(mine),
+                "samples_under_load": sum(1 for p in pw if p >= 300.0),
+                "power_w_median": statistics.median(pw) if pw else None, "window": window}
 
 
 def _gpu_uuid(dev: int) -> str:
@@ -177,12 +204,8 @@ def gemm_shapes():
     return [(M, K, N) for M in SD15_M for (K, N) in SD15_KN]
 
 
-def attn_blocks(world: int):
-    """Per-rank attention blocks: the global block has batch 2*world; this rank owns 2 batches."""
-    return [(B, H, Sq, Skv, D) for (B, H, Sq, Skv, D) in ATTN_BLOCKS]
-
-
-def step_flops(world: int = 1) -> tuple[float, float]:
+def step_flops() -> tuple[float, float]:
+    """(GEMM, attention) algorithmic FLOPs of one rank's step."""
     g = sum(2.0 * M * K * N for M, K, N in gemm_shapes())
     a = sum(4.0 * B * H * Sq * Skv * D for B, H, Sq, Skv, D in ATTN_BLOCKS)
     return g, a
@@ -194,6 +217,14 @@ def _seeded(shape, std, seed, device, dtype=torch.bfloat16):
     return t.to(device=device, dtype=dtype)
 
 
+def _gemm_seed(rank: int, i: int) -> int:
+    return 1000 * rank + 3 * i
+
+
+def _attn_seed(rank: int, j: int) -> int:
+    return 500000 + 1000 * rank + 7 * j
+
+
 class GpuWorkload:
     def __init__(self, device: torch.device, rank: int, world: int):
         from npu_ai_b200 import kernels
@@ -202,7 +233,7 @@ class GpuWorkload:
         self.world = world
         self.gemms = []
         for i, (M, K, N) in enumerate(gemm_shapes()):
-            s = 1000 * rank + 3 * i
+            s = _gemm_seed(rank, i)
             x = _seeded((M, K), 1.0, s, device)
             w = _seeded((N, K), 0.02, s + 1, device)
             b = _seeded((N,), 0.01, s + 2, device)
@@ -211,48 +242,53 @@ class GpuWorkload:
             self.gemms.append((x, w, b, out, h, 2.0 * M * K * N, 2 * (M * K + N * K + N + M * N)))
         self.attn = []
         for j, (B, H, Sq, Skv, D) in enumerate(ATTN_BLOCKS):
-            s = 500000 + 1000 * rank + 7 * j
+            s = _attn_seed(rank, j)
             q = _seeded((B, Sq, H * D), 1.0, s, device)
             kk = _seeded((B, Skv, H * D), 1.0, s + 1, device)
             v = _seeded((B, Skv, H * D), 1.0, s + 2, device)
             out = torch.empty((B, Sq, H * D), dtype=torch.bfloat16, device=device)
             full = torch.empty((B * world, Sq, H * D), dtype=torch.bfloat16, device=device) if world > 1 else None
             self.attn.append((q, kk, v, out, full, H, 4.0 * B * H * Sq * Skv * D))
-        self.working_set = sum(t.numel() * t.element_size() for g in self.gemms for t in g[:4]) + \
-            sum(t.numel() * t.element_size() for a in self.attn for t in a[:4])
+        self.comm = torch.cuda.Stream(device) if world > 1 else None
 
     def step(self, dist, events=None):
-        """One pass. `events` (pre-created timing events, see make_events) marks the start of each M group of the
-        sweep (the sweep runs in M order), the end of the GEMM launches (the start of the attention launches) and
-        the end of the attention launches: only segment boundaries carry an event, so the launches inside a segment
-        keep their programmatic-dependent-launch overlap."""
+        """One pass: the attention blocks, then the GEMM sweep in M order. With N > 1 ranks each attention output
+        is all-gathered on the communication stream while the sweep runs; the step joins it at the end.
+
+        `events` (see make_events) marks the start of every attention block, the start of every M group of the
+        sweep and the end of the step. Only boundaries carry an event, so launches inside an M group keep their
+        programmatic-dependent-launch overlap."""
         k = self.k
-        groups = self.m_groups()
-        group = -1
-        for (x, w, b, out, h, _, _) in self.gemms:
-            if events is not None and groups.index(x.shape[0]) != group:
-                group = groups.index(x.shape[0])
-                events[group].record()
-            k.gemm(x, w, b, out=out, handle=h)
-        if events is not None:
-            events[len(groups)].record()
+        main = torch.cuda.current_stream(self.device)
+        ei = 0
         for (q, kk, v, out, full, H, _) in self.attn:
+            if events is not None:
+                events[ei].record()
+                ei += 1
             k.attention(q, kk, v, H, out=out)
             if full is not None:
-                dist.pg.all_gather_into_tensor(full, out)
+                self.comm.wait_stream(main)
+                with torch.cuda.stream(self.comm):
+                    dist.pg.all_gather_into_tensor(full, out)
+        group = None
+        for (x, w, b, out, h, _, _) in self.gemms:
+            if events is not None and x.shape[0] != group:
+                group = x.shape[0]
+                events[ei].record()
+                ei += 1
+            k.gemm(x, w, b, out=out, handle=h)
+        if self.comm is not None:
+            main.wait_stream(self.comm)
         if events is not None:
-            events[len(groups) + 1].record()
+            events[ei].record()
 
     def m_groups(self) -> list[int]:
-        seen = []
-        for g in self.gemms:
-            if g[0].shape[0] not in seen:
-                seen.append(g[0].shape[0])
-        return seen
+        return list(dict.fromkeys(g[0].shape[0] for g in self.gemms))
 
-    def make_events(self, external: bool = False) -> list:
-        """[start of M group 0, 1, ..., GEMM end = attention start, attention end]"""
-        return [torch.cuda.Event(enable_timing=True, external=external) for _ in range(len(self.m_groups()) + 2)]
+    def make_events(self) -> list:
+        """[start of attention block 0..3, start of M group 0..5, end of step]"""
+        return [torch.cuda.Event(enable_timing=True, external=True)
+                for _ in range(len(self.attn) + len(self.m_groups()) + 1)]
 
     def capture(self, dist, events=None) -> torch.cuda.CUDAGraph:
         """One step captured as a CUDA graph (kernels launched back to back by the GPU, no host in the loop). The
@@ -277,7 +313,7 @@ class GpuWorkload:
 
 
 class E2EWorkload:
-    """The same step through the public API (NpuGemm) with pinned host inputs and outputs."""
+    """The same step through the public API (NpuGemm) with pinned host inputs, biases and outputs."""
 
     def __init__(self, device: torch.device, rank: int, world: int):
         from npu_ai_b200.runner import NpuGemm
@@ -288,17 +324,17 @@ class E2EWorkload:
         self.h2d = 0
         self.d2h = 0
         for i, (M, K, N) in enumerate(gemm_shapes()):
-            s = 1000 * rank + 3 * i
+            s = _gemm_seed(rank, i)
             x = _seeded((M, K), 1.0, s, "cpu").pin_memory()
             w = self.rt.upload_weight(_seeded((N, K), 0.02, s + 1, "cpu"), layout="nk")
-            b = _seeded((N,), 0.01, s + 2, device)
+            b = _seeded((N,), 0.01, s + 2, "cpu").pin_memory()
             y = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
             self.gemms.append((x, w, b, y))
-            self.h2d += x.numel() * 2
+            self.h2d += (x.numel() + b.numel()) * 2
             self.d2h += y.numel() * 2
         self.attn = []
         for j, (B, H, Sq, Skv, D) in enumerate(ATTN_BLOCKS):
-            s = 500000 + 1000 * rank + 7 * j
+            s = _attn_seed(rank, j)
             q, kk, v = (_seeded((B, S, H * D), 1.0, s + t, "cpu").pin_memory()
                         for t, S in ((0, Sq), (1, Skv), (2, Skv)))
             y = torch.empty((B * world, Sq, H * D), dtype=torch.bfloat16).pin_memory()
@@ -321,14 +357,14 @@ class E2EWorkload:
         rt = self.rt
         if not hasattr(self, "d2h_stream"):
             self.d2h_stream = torch.cuda.Stream(self.device)
-        for (x, w, b, y) in self.gemms:
-            self._out(rt.linear(x, w, b), y)  # host x -> device and the GEMM on the current stream
         for (q, kk, v, H, y, full) in self.attn:
             o = rt.attention(q, kk, v, H)
             if full is not None:
                 dist.pg.all_gather_into_tensor(full, o)
                 o = full
             self._out(o, y)
+        for (x, w, b, y) in self.gemms:
+            self._out(rt.linear(x, w, b), y)  # host x and bias -> device, and the GEMM, on the current stream
         # The step ends when the last result is in host memory.
         torch.cuda.current_stream(self.device).wait_stream(self.d2h_stream)
 
@@ -337,8 +373,10 @@ class E2EWorkload:
 # CPU path (the reference's CPU fallback semantics, via the oracle)
 # ----------------------------------------------------------------------------------------------------------------
 def _cpu_ops():
-    """The step's 70 ops in a fixed interleaved order (large and small alternate, so a prefix is representative)."""
-    ops = [("gemm", s) for s in gemm_shapes()] + [("attn", a) for a in ATTN_BLOCKS]
+    """The step's 70 ops in a fixed interleaved order (large and small alternate, so a prefix is representative).
+    Each op carries the seed its GPU counterpart uses on rank 0."""
+    ops = [("gemm", s, _gemm_seed(0, i)) for i, s in enumerate(gemm_shapes())] + \
+        [("attn", a, _attn_seed(0, j)) for j, a in enumerate(ATTN_BLOCKS)]
     ops.sort(key=lambda o: (o[1][0] * o[1][1] * o[1][2]) if o[0] == "gemm" else o[1][2] * o[1][3] * o[1][4] * 16)
     inter = []
     lo, hi = 0, len(ops) - 1
@@ -350,35 +388,41 @@ def _cpu_ops():
     return inter
 
 
-def _cpu_run_op(op, seed):
-    from oracle import attention_ref, linear_ref
-    kind, shp = op
+def _cpu_inputs(op):
+    kind, shp, seed = op
     if kind == "gemm":
         M, K, N = shp
-        x = _seeded((M, K), 1.0, seed, "cpu")
-        w = _seeded((N, K), 0.02, seed + 1, "cpu")
-        b = _seeded((N,), 0.01, seed + 2, "cpu")
-        t0 = time.perf_counter()
-        linear_ref(x, w, b)
+        return (_seeded((M, K), 1.0, seed, "cpu"), _seeded((N, K), 0.02, seed + 1, "cpu"),
+                _seeded((N,), 0.01, seed + 2, "cpu"))
+    B, H, Sq, Skv, D = shp
+    return (_seeded((B, Sq, H * D), 1.0, seed, "cpu"), _seeded((B, Skv, H * D), 1.0, seed + 1, "cpu"),
+            _seeded((B, Skv, H * D), 1.0, seed + 2, "cpu"))
+
+
+def _cpu_run(op, inputs) -> tuple[float, float]:
+    """Run one op of the step on the host cores: (seconds, algorithmic FLOPs)."""
+    from oracle import attention_ref, linear_ref
+    kind, shp, _ = op
+    t0 = time.perf_counter()
+    if kind == "gemm":
+        linear_ref(*inputs)
+        M, K, N = shp
         return time.perf_counter() - t0, 2.0 * M * K * N
     B, H, Sq, Skv, D = shp
-    q = _seeded((B, Sq, H * D), 1.0, seed, "cpu")
-    k = _seeded((B, Skv, H * D), 1.0, seed + 1, "cpu")
-    v = _seeded((B, Skv, H * D), 1.0, seed + 2, "cpu")
-    t0 = time.perf_counter()
-    attention_ref(q, k, v, H)
+    attention_ref(*inputs, H)
     return time.perf_counter() - t0, 4.0 * B * H * Sq * Skv * D
 
 
 def cpu_baseline(budget_s: float = 20.0) -> dict:
     """One pass over the step's ops on the host cores (stops early past the time budget)."""
     torch.set_num_threads(os.cpu_count() or 1)
-    _cpu_run_op(("gemm", (64, 64, 64)), 1)
+    warm = ("gemm", (64, 64, 64), 1)
+    _cpu_run(warm, _cpu_inputs(warm))
     tot_t = tot_f = 0.0
     n = 0
     ops = _cpu_ops()
-    for i, op in enumerate(ops):
-        dt, fl = _cpu_run_op(op, 7 + 3 * i)
+    for op in ops:
+        dt, fl = _cpu_run(op, _cpu_inputs(op))
         tot_t += dt
         tot_f += fl
         n += 1
@@ -391,29 +435,34 @@ def cpu_baseline(budget_s: float = 20.0) -> dict:
 
 
 def run_reference(args) -> None:
-    """--impl reference: the reference's CPU path on the host cores, each step one op of the hot-path step."""
+    """--impl reference: the reference's CPU path (the oracle port: F.linear / SDPA in f32 on bf16-rounded inputs,
+    the reference's CPU fallback) on the host cores. Each bench step is the whole 70-op hot-path step on the same
+    seeded inputs as the GPU arm's rank 0; inputs are generated once, outside the timed region."""
     torch.set_num_threads(os.cpu_count() or 1)
     ops = _cpu_ops()
-    for i in range(args.warmup):
-        _cpu_run_op(ops[i % len(ops)], 11 + i)
+    inputs = [_cpu_inputs(op) for op in ops]
+    warm = ("gemm", (64, 64, 64), 1)
+    _cpu_run(warm, _cpu_inputs(warm))
+    for _ in range(args.warmup):
+        for op, inp in zip(ops, inputs):
+            _cpu_run(op, inp)
     tot_t = tot_f = 0.0
-    for i in range(args.steps):
-        dt, fl = _cpu_run_op(ops[i % len(ops)], 7 + 3 * i)
-        tot_t += dt
-        tot_f += fl
+    for _ in range(args.steps):
+        for op, inp in zip(ops, inputs):
+            dt, fl = _cpu_run(op, inp)
+            tot_t += dt
+            tot_f += fl
     value = tot_f / tot_t / 1e12
     n = args.steps
+    sample = (f"the whole {len(ops)}-op step ({tot_f / n / 1e9:.0f} GFLOP) per bench step: torch CPU F.linear / SDPA "
+              "in f32 on bf16-rounded inputs, the reference's CPU fallback (comfyui node :151, "
+              "scripts/11-attn-fused-test.py:115-119)")
     line = {"metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": n,
             "warmup": args.warmup, "ms_per_step": round(tot_t / n * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16-rounded inputs)", "data": "synthetic",
-            "impl": "reference",
-            "config": {"workload": "sd15-linear-sweep+attention-blocks", "gemm_shapes": len(gemm_shapes()),
-                       "attention_blocks": ATTN_BLOCKS},
+            "impl": "reference", "config": hotpath_config(args.gpus),
             "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-                             "kind": "port",
-                             "sample": f"{n} ops of the 70-op step cycled one per step (interleaved large/small): "
-                                       "torch CPU F.linear / SDPA in f32 on bf16-rounded inputs, the reference's "
-                                       "CPU fallback (comfyui node :151, scripts/11-attn-fused-test.py:115-119)"},
+                             "kind": "port", "sample": sample},
             "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -421,6 +470,55 @@ def run_reference(args) -> None:
 # ----------------------------------------------------------------------------------------------------------------
 # our arm
 # ----------------------------------------------------------------------------------------------------------------
+def _time_graph(g: torch.cuda.CUDAGraph, replays: int) -> float:
+    """ms per replay of a graph, CUDA events on the current stream."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / replays
+
+
+def config1_roofline(device, peaks) -> dict:
+    """Config 1 (x [4096x320] . W[320x320]^T + b, bf16 out) as a standalone sequence: 48 launches over rotating x
+    and out buffers (252 MB, twice the L2) with one resident weight, captured as a CUDA graph (PDL between the
+    launches, as in a model's chain of Linears)."""
+    from npu_ai_b200 import kernels
+    M, K, N = CONFIG1
+    copies = 48
+    xs = [_seeded((M, K), 1.0, 77 + i, device) for i in range(copies)]
+    outs = [torch.empty((M, N), dtype=torch.bfloat16, device=device) for _ in range(copies)]
+    w = _seeded((N, K), 0.02, 7, device)
+    b = _seeded((N,), 0.01, 8, device)
+    h = kernels.register_weight(w)
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        for x, o in zip(xs, outs):
+            kernels.gemm(x, w, b, out=o, handle=h)
+    torch.cuda.current_stream(device).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for x, o in zip(xs, outs):
+            kernels.gemm(x, w, b, out=o, handle=h)
+    for _ in range(3):
+        g.replay()
+    us = _time_graph(g, 10) * 1e3 / copies
+    kernels.check_status(device)
+    del g
+    kernels.release_weight(h)
+    flops = 2.0 * M * K * N
+    nbytes = 2 * (M * K + N * K + N + M * N)
+    ideal_us = nbytes / (peaks["hbm_gbs"] * 1e3)
+    return {"shape": "4096x320x320 + bias, bf16 out", "us": round(us, 3), "tflops": round(flops / us / 1e6, 1),
+            "gbs": round(nbytes / us / 1e3, 1), "hbm_roofline_us": round(ideal_us, 3),
+            "frac_of_roofline": round(ideal_us / us, 4), "bound": "hbm",
+            "timing": f"CUDA graph of {copies} launches over rotating buffers ({copies * 2 * M * K * 2 / 2**20:.0f} MiB "
+                      "of x and out, larger than L2), 10 replays, CUDA events"}
+
+
 def run_ours(args, dist) -> None:
     from npu_ai_b200 import kernels
     device = torch.device("cuda", dist.local_rank)
@@ -432,97 +530,119 @@ def run_ours(args, dist) -> None:
     torch.cuda.synchronize()
     kernels.check_status(device)
 
-    uuids = [_gpu_uuid(dist.local_rank)]
-    sampler = ClockSampler(uuids) if dist.rank == 0 else None
-    # The step runs as a CUDA graph. A twin graph carries timing events at the boundaries of its GEMM and attention
-    # segments; it runs as the last step of the timed region, giving the average device time of each kind of launch
-    # inside a real step (segment time / launches in it).
+    sampler = ClockSampler([_gpu_uuid(dist.local_rank)]) if dist.rank == 0 else None
+    if sampler is not None:
+        sampler.start()
+    # The step runs as a CUDA graph. A twin graph carries timing events at the attention-block and GEMM M-group
+    # boundaries; it runs as the last step of the timed region.
     graph = wl.capture(dist)
-    events = wl.make_events(external=True)
+    events = wl.make_events()
     graph_ev = wl.capture(dist, events)
     for _ in range(2):
         graph.replay()
     graph_ev.replay()
     torch.cuda.synchronize()
     kernels.check_status(device)
+    # Soak: replays for about 4.5 s right before the timed region, so the clock record holds enough samples of the
+    # GPU under this load (every rank replays the same count: the graphs hold collectives).
+    one = _time_graph(graph, 3)
+    soak = int(dist.max(float(min(20000, max(10, round(args.soak_s * 1e3 / max(one, 1e-3))))), device))
     dist.barrier()
     torch.cuda.synchronize()
-    if sampler is not None:
-        sampler.start()
-        time.sleep(0.3)
+    t_soak = time.perf_counter()
+    for _ in range(soak):
+        graph.replay()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    dist.barrier()
-    torch.cuda.synchronize()
-    if sampler is not None:
-        sampler.mark(True)
     t0.record()
     for _ in range(args.steps - 1):
         graph.replay()
     graph_ev.replay()
     t1.record()
     torch.cuda.synchronize()
-    if sampler is not None:
-        sampler.mark(False)
+    t_end = time.perf_counter()
     dist.barrier()
-    clocks = sampler.stop() if sampler is not None else None
+    clocks = sampler.summary(t_soak, t_end, f"{soak} step replays ({soak * one / 1e3:.1f} s) directly before the "
+                                           "timed region, then the timed region") if sampler is not None else None
     kernels.check_status(device)
     ms_local = t0.elapsed_time(t1) / args.steps
     ms = dist.max(ms_local, device)
-    n_groups = len(wl.m_groups())
-    gemm_ms = events[0].elapsed_time(events[n_groups])
-    attn_ms = events[n_groups].elapsed_time(events[n_groups + 1])
-    by_m = {}
-    for gi, M in enumerate(wl.m_groups()):
-        g_ms = events[gi].elapsed_time(events[gi + 1])
-        g_fl = sum(g[5] for g in wl.gemms if g[0].shape[0] == M)
-        by_m[str(M)] = {"us": round(g_ms * 1e3, 1), "tflops": round(g_fl / (g_ms / 1e3) / 1e12, 1)}
     gflops, aflops = step_flops()
     total = (gflops + aflops) * dist.world
     value = total / (ms / 1e3) / 1e12
 
-    # dominant kernel: the GEMM (most of the step's FLOPs and time)
+    na = len(wl.attn)
+    groups = wl.m_groups()
+    seg = [events[i].elapsed_time(events[i + 1]) for i in range(len(events) - 1)]
+    attn_ms = sum(seg[:na])
+    gemm_ms = sum(seg[na:])
+    peak = peaks["bf16_tflops"]
+    hbm = peaks["hbm_gbs"]
+    by_m = {}
+    for gi, M in enumerate(groups):
+        g_ms = seg[na + gi]
+        mine = [g for g in wl.gemms if g[0].shape[0] == M]
+        g_fl = sum(g[5] for g in mine)
+        ideal_ms = sum(max(g[5] / (peak * 1e12), g[6] / (hbm * 1e9)) for g in mine) * 1e3
+        by_m[str(M)] = {"us": round(g_ms * 1e3, 1), "tflops": round(g_fl / (g_ms / 1e3) / 1e12, 1),
+                        "frac": round(g_fl / (g_ms / 1e3) / 1e12 / peak, 4),
+                        "frac_of_roofline": round(ideal_ms / g_ms, 4),
+                        "roofline_bound": "tensor" if all(g[5] / peak / 1e3 >= g[6] / hbm for g in mine) else
+                        ("hbm" if all(g[5] / peak / 1e3 < g[6] / hbm for g in mine) else "mixed")}
+    attn_blocks = {}
+    for j, (B, H, Sq, Skv, D) in enumerate(ATTN_BLOCKS):
+        a_ms = seg[j]
+        fl = 4.0 * B * H * Sq * Skv * D
+        mufu_us = B * H * Sq * Skv / (SMS * EX2_PER_CLK_PER_SM * peaks["sm_max_mhz"] * 1e6) * 1e6
+        attn_blocks[f"{B}x{H}x{Sq}x{Skv}x{D}"] = {
+            "us": round(a_ms * 1e3, 1), "tflops": round(fl / (a_ms / 1e3) / 1e12, 1),
+            "frac": round(fl / (a_ms / 1e3) / 1e12 / peak, 4), "mufu_floor_us": round(mufu_us, 1),
+            "bytes": 2 * B * H * D * (2 * Sq + 2 * Skv)}
+
     gemm_bytes = sum(g[6] for g in wl.gemms)
     achieved = gflops / (gemm_ms / 1e3) / 1e12
-    peak = peaks["bf16_tflops_sustained"]
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "peak_kind": f"{peaks['source']} sustained bf16 (cuBLAS loop)",
+                "frac": round(achieved / peak, 4),
+                "peak_kind": f"{peaks['source']} burst bf16 (cuBLAS 8192^3, best of 10): the timed region is "
+                             f"{args.steps} steps of about {ms:.2f} ms",
+                "frac_of_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4),
                 "kernel": "gemm_bf16_tcgen05_kernel (66 sweep launches per step)",
                 "algorithmic_bytes_per_launch": int(gemm_bytes / len(wl.gemms)),
                 "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean per sweep launch "
+                                  "(profiles/gemm_sweep_dram.md)",
                 "gemm_launch_us": round(gemm_ms * 1e3 / len(wl.gemms), 3),
                 "gemm_ms_per_step": round(gemm_ms, 4),
-                "attention_ms_per_step": round(attn_ms, 4),  # with N > 1 this segment includes the all-gathers
-                "gemm_by_m": {m: dict(v, frac=round(v["tflops"] / peak, 4)) for m, v in by_m.items()},
+                "attention_ms_per_step": round(attn_ms, 4),
+                "gemm_by_m": by_m,
                 "gemm_tflops": round(achieved, 1),
-                "attention_tflops": round(aflops / (attn_ms / 1e3) / 1e12, 1) if attn_ms else None,
-                "timing": "CUDA events at the GEMM and attention segment boundaries of the timed region's last step "
-                          "(graph replay); average launch duration = segment time / launches"}
+                "attention_tflops": round(aflops / (attn_ms / 1e3) / 1e12, 1),
+                "attention_blocks": attn_blocks,
+                "config1": config1_roofline(device, peaks),
+                "timing": "CUDA events at the attention-block and GEMM M-group boundaries of the timed region's "
+                          "last step (graph replay); average launch duration = segment time / launches"}
 
-    # end to end through the public API, host buffers
-    e2e = None
-    if not args.no_e2e:
-        e2e = run_e2e(args, dist, device, total)
+    e2e = None if args.no_e2e else run_e2e(args, dist, device, total)
     kernels.check_status(device)
+    del graph, graph_ev  # graphs holding NCCL calls go before the process group
+    wl.release()
+    del wl
+    torch.cuda.empty_cache()
+
+    unet = None if args.no_unet else unet_leg(args, dist, device, sampler)
+    if sampler is not None:
+        sampler.stop()
 
     cpu = cpu_baseline() if (dist.rank == 0 and dist.world == 1 and not args.no_cpu) else None
     if dist.rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world,
                 "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic",
-                "config": {"workload": "sd15-linear-sweep+attention-blocks",
-                           "gemm_shapes": "M{77,154,256,1024,4096,8192} x 11 SD1.5 (K,N), bf16 out, bias",
-                           "attention_blocks": ATTN_BLOCKS, "per_rank_attention_batch": 2,
-                           "parallelism": f"replicas(gemm)+pairs-sharded(attention) x{dist.world}",
-                           "l2": f"inputs larger than L2: {wl.working_set / 2**20:.0f} MiB touched once per step "
-                                 f"vs {L2_BYTES / 2**20:.0f} MiB L2"},
-                "gpu_launches": wl.launches_per_step() * args.steps,
+                "data": "synthetic", "config": hotpath_config(dist.world),
+                "gpu_launches": (len(ATTN_BLOCKS) + len(gemm_shapes())) * args.steps,
                 "execution": "CUDA graph of the step (PDL between kernels), replayed per step",
-                "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks}
+                "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "unet": unet}
         print(json.dumps(line), flush=True)
-    del graph, graph_ev  # graphs holding NCCL calls go before the process group
-    wl.release()
 
 
 def run_e2e(args, dist, device, total_flops) -> dict:
@@ -543,13 +663,14 @@ def run_e2e(args, dist, device, total_flops) -> dict:
     e2e_ms = dist.max(s0.elapsed_time(s1) / e2e_steps, device)
     return {"value": round(total_flops / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
             "h2d_bytes_per_step": int(e2e_wl.h2d), "d2h_bytes_per_step": int(e2e_wl.d2h),
-            "ms_per_step": round(e2e_ms, 3), "api": "npu_ai_b200.runner.NpuGemm.linear / .attention",
-            "copies": "host inputs copied by the API on the compute stream; results copied out on a second stream, "
-                      "overlapping the next ops"}
+            "ms_per_step": round(e2e_ms, 3), "steps": e2e_steps,
+            "api": "npu_ai_b200.runner.NpuGemm.linear / .attention",
+            "copies": "host inputs and biases copied by the API on the compute stream; results copied out on a second "
+                      "stream, overlapping the next ops"}
 
 
 # ----------------------------------------------------------------------------------------------------------------
-# UNet workload: SD1.5-architecture UNet denoise steps (batch 2 with 4 Euler steps; batch 16, sharded over GPUs)
+# UNet: SD1.5-architecture UNet denoise steps (batch 16 sharded over the ranks; batch 2 with 4 Euler steps)
 # ----------------------------------------------------------------------------------------------------------------
 def _kernel_kind(name: str) -> str:
     if "attention_fwd" in name:
@@ -596,126 +717,186 @@ def kernel_times(replay, steps: int = 3) -> str:
     return "\n".join(lines)
 
 
-def run_unet(args, dist) -> None:
-    """Euler CFG denoise steps of a random-init SD1.5-architecture UNet with every Linear and attention on the B200
-    kernels (through the ComfyUI node runtime). The batch (prompts x CFG pair) is sharded over the ranks with each
-    prompt's pair local; latents are all-gathered over NCCL every step. One step = one UNet call on the whole batch
-    plus the guidance combine and the Euler update, captured as a CUDA graph. Strong scaling: the total batch is
-    fixed as GPUs are added."""
-    from npu_ai_b200 import comfy_nodes as cn
-    from npu_ai_b200 import kernels
-    from npu_ai_b200.sd15_unet import build_unet, karras_sigmas, prompt_shard, seeded_prompts, sigma_to_t
-    device = torch.device("cuda", dist.local_rank)
-    torch.cuda.set_device(device)
-    P = args.batch // 2
-    lo, hi = prompt_shard(P, dist.world, dist.rank)
-    if hi - lo < 1:
-        raise SystemExit("need at least one prompt (two images: uncond + cond) per rank")
-    model = build_unet(seed=0, device=device, dtype=torch.bfloat16)
-    # Channels-last activations: cuDNN's tensor-core convolutions take NHWC directly, and the transformer blocks'
-    # (b, c, h, w) -> (b, hw, c) reshapes become views.
-    model.to(memory_format=torch.channels_last)
-    rt = cn._get_runtime(device)
-    rt.min_tokens = 64
-    rt.take_over(model, 320, ("time_embed", "label_emb", "emb_layers"))
-    rt.attn.mode = "gpu"
-    rt.attn.min_tokens = 64
-    rt.enabled = True
-    to = {"optimized_attention_override": cn._gpu_attention_override}
-    lat, ctx, unc = seeded_prompts(P, args.latent, seed=1, device=device, dtype=torch.bfloat16)
-    lat, ctx, unc = lat[lo:hi].contiguous(), ctx[lo:hi].contiguous(), unc[lo:hi].contiguous()
-    cond = torch.cat([unc, ctx])
-    sigmas = karras_sigmas(args.unet_steps).to(device)
-    sig = torch.zeros(2, device=device)  # [sigma, sigma_next] of the step being replayed
-    x = (lat.float() * sigmas[0]).contiguous()
-    full = torch.empty((P, *lat.shape[1:]), dtype=torch.float32, device=device) if dist.world > 1 else None
+class UNetBench:
+    """Euler CFG denoise steps of a random-init SD1.5-architecture UNet with every Linear, attention, convolution
+    and normalisation the node takes over on the B200 kernels (through the ComfyUI node runtime). The batch
+    (prompts x CFG pair) is sharded over the ranks with each prompt's pair local; latents are all-gathered over NCCL
+    every step. One step = one UNet call on the rank's batch plus the guidance combine and the Euler update,
+    captured as a CUDA graph. Strong scaling: the total batch is fixed as GPUs are added."""
 
-    def step():
-        s, s_next = sig[0], sig[1]
-        x_in = (torch.cat([x, x]) / torch.sqrt(s * s + 1.0)).to(torch.bfloat16).contiguous(
-            memory_format=torch.channels_last)
-        t = sigma_to_t(s).expand(x_in.shape[0])
-        eps = model(x_in, t, cond, to).float()
-        eu, ec = eps.chunk(2)
-        x.add_((s_next - s) * (eu + 7.5 * (ec - eu)))
-        if full is not None:
-            dist.pg.all_gather_into_tensor(full, x)
+    def __init__(self, dist, device):
+        from npu_ai_b200 import comfy_nodes as cn
+        from npu_ai_b200.sd15_unet import build_unet
+        self.dist, self.device = dist, device
+        self.model = build_unet(seed=0, device=device, dtype=torch.bfloat16)
+        # Channels-last activations: the convolution kernels take NHWC directly, and the transformer blocks'
+        # (b, c, h, w) -> (b, hw, c) reshapes become views.
+        self.model.to(memory_format=torch.channels_last)
+        self.rt = cn._get_runtime(device)
+        self.rt.min_tokens = 64
+        self.rt.take_over(self.model, 320, ("time_embed", "label_emb", "emb_layers"))
+        self.rt.attn.mode = "gpu"
+        self.rt.enabled = True
+        self.to = {"optimized_attention_override": cn._gpu_attention_override}
 
-    def set_step(i):
-        i %= args.unet_steps
-        sig.copy_(torch.stack([sigmas[i], sigmas[i + 1]]))
+    def measure(self, batch: int, latent: int, steps: int, warmup: int, unet_steps: int = 4,
+                sampler: ClockSampler | None = None, kernel_times_out: bool = False) -> dict:
+        from npu_ai_b200 import kernels
+        from npu_ai_b200.sd15_unet import karras_sigmas, prompt_shard, seeded_prompts, sigma_to_t
+        dist, device = self.dist, self.device
+        P = batch // 2
+        lo, hi = prompt_shard(P, dist.world, dist.rank)
+        if hi - lo < 1:
+            raise SystemExit("need at least one prompt (two images: uncond + cond) per rank")
+        lat, ctx, unc = seeded_prompts(P, latent, seed=1, device=device, dtype=torch.bfloat16)
+        lat, ctx, unc = lat[lo:hi].contiguous(), ctx[lo:hi].contiguous(), unc[lo:hi].contiguous()
+        cond = torch.cat([unc, ctx])
+        sigmas = karras_sigmas(unet_steps).to(device)
+        sig = torch.zeros(2, device=device)  # [sigma, sigma_next] of the step being replayed
+        x = (lat.float() * sigmas[0]).contiguous()
+        # uneven shards are padded to the largest one for a single all-gather
+        width = -(-P // dist.world)
+        pad = torch.zeros((width, *lat.shape[1:]), dtype=torch.float32, device=device) if dist.world > 1 else None
+        full = torch.empty((width * dist.world, *lat.shape[1:]), dtype=torch.float32, device=device) \
+            if dist.world > 1 else None
+        model, to = self.model, self.to
 
-    with torch.no_grad():
-        for i in range(max(3, args.warmup)):
-            set_step(i)
-            step()
-        torch.cuda.synchronize()
-        cs = torch.cuda.Stream(device)
-        cs.wait_stream(torch.cuda.current_stream(device))
-        with torch.cuda.stream(cs):
-            step()
-        torch.cuda.current_stream(device).wait_stream(cs)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=cs):
-            step()
-        torch.cuda.synchronize()
-        kernels.check_status(device)
-        dist.barrier()
-        sampler = ClockSampler([_gpu_uuid(dist.local_rank)]) if dist.rank == 0 else None
+        def step():
+            s, s_next = sig[0], sig[1]
+            x_in = (torch.cat([x, x]) / torch.sqrt(s * s + 1.0)).to(torch.bfloat16).contiguous(
+                memory_format=torch.channels_last)
+            t = sigma_to_t(s).expand(x_in.shape[0])
+            eps = model(x_in, t, cond, to).float()
+            eu, ec = eps.chunk(2)
+            x.add_((s_next - s) * (eu + 7.5 * (ec - eu)))
+            if full is not None:
+                pad[: hi - lo].copy_(x)
+                dist.pg.all_gather_into_tensor(full, pad)
+
+        def set_step(i):
+            i %= unet_steps
+            sig.copy_(torch.stack([sigmas[i], sigmas[i + 1]]))
+
+        with torch.no_grad():
+            for i in range(max(3, warmup)):
+                set_step(i)
+                step()
+            torch.cuda.synchronize()
+            cs = torch.cuda.Stream(device)
+            cs.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(cs):
+                step()
+            torch.cuda.current_stream(device).wait_stream(cs)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cs):
+                step()
+            torch.cuda.synchronize()
+            kernels.check_status(device)
+            for i in range(3):
+                set_step(i)
+                g.replay()
+            dist.barrier()
+            torch.cuda.synchronize()
+            tb = time.perf_counter()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for i in range(steps):
+                set_step(i)
+                g.replay()
+            t1.record()
+            torch.cuda.synchronize()
+            te = time.perf_counter()
+            dist.barrier()
+            kernels.check_status(device)
+            kt = kernel_times(g.replay) if (kernel_times_out and dist.world == 1) else None
+        ms = dist.max(t0.elapsed_time(t1) / steps, device)
+        del g
+        torch.cuda.empty_cache()
+        out = {"batch": batch, "latent": latent, "per_rank_batch": 2 * (hi - lo), "ms_per_step": round(ms, 3),
+               "steps_per_s": round(1e3 / ms, 3), "s_per_image": round(ms * unet_steps / 1e3 / P, 5),
+               "euler_steps_per_image": unet_steps, "steps": steps}
         if sampler is not None:
-            sampler.start()
-            time.sleep(0.3)
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        dist.barrier()
-        torch.cuda.synchronize()
-        if sampler is not None:
-            sampler.mark(True)
-        t0.record()
-        for i in range(args.steps):
-            set_step(i)
-            g.replay()
-        t1.record()
-        torch.cuda.synchronize()
-        if sampler is not None:
-            sampler.mark(False)
-        dist.barrier()
-        clocks = sampler.stop() if sampler is not None else None
-        kernels.check_status(device)
-        if args.kernel_times and dist.world == 1:
-            print(kernel_times(g.replay), file=sys.stderr, flush=True)
-    ms = dist.max(t0.elapsed_time(t1) / args.steps, device)
-    cpu = None
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+            out["clocks"] = sampler.summary(tb, te, "the timed region")
+        if kt is not None:
+            out["kernel_times"] = kt
+        return out
+
+    def cpu_baseline(self, latent: int) -> dict:
+        """One batch-2 (one prompt x CFG) UNet call of the same architecture in f32 on the host cores with torch's
+        CPU F.linear / SDPA / conv (the reference's CPU fallback)."""
+        from npu_ai_b200.sd15_unet import build_unet, seeded_prompts
         torch.set_num_threads(os.cpu_count() or 1)
         cpu_model = build_unet(seed=0, device="cpu", dtype=torch.bfloat16).float()
-        xc = torch.cat([lat, lat]).float().cpu()
-        tc = torch.full((xc.shape[0],), 500.0)
+        lat, ctx, unc = seeded_prompts(1, latent, seed=1)
+        xc = torch.cat([lat, lat]).bfloat16().float()
+        cond = torch.cat([unc, ctx]).bfloat16().float()
+        tc = torch.full((2,), 500.0)
         with torch.no_grad():
-            cpu_model(xc[:, :, :8, :8], tc, cond.float().cpu())
+            cpu_model(xc[:, :, :8, :8], tc, cond)
             c0 = time.perf_counter()
-            cpu_model(xc, tc, cond.float().cpu())
+            cpu_model(xc, tc, cond)
             cdt = time.perf_counter() - c0
-        cpu = {"value": round(1.0 / cdt, 4), "unit": "steps/s", "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"one UNet call (batch {xc.shape[0]}, {args.latent}x{args.latent} latent) in f32 on the "
-                         f"host with torch's CPU F.linear/SDPA (the reference's CPU fallback): {cdt:.2f} s"}
+        return {"value": round(1.0 / cdt, 4), "unit": "steps/s (batch 2)", "cores": torch.get_num_threads(),
+                "kind": "port", "ms_per_step_batch2": round(cdt * 1e3, 1),
+                "s_per_image": round(cdt * 4 / 1, 3),
+                "sample": f"one batch-2 UNet call ({latent}x{latent} latent) in f32 on the host with torch's CPU "
+                          f"F.linear / SDPA / conv (the reference's CPU fallback): {cdt:.2f} s; the batch-16 step "
+                          f"is 8 such calls ({8 * cdt:.1f} s, extrapolated per prompt)"}
+
+
+def unet_leg(args, dist, device, sampler) -> dict:
+    """The UNet object of the driver's line: batch 16 on every latent of --unet-latents, sharded over the ranks;
+    at N = 1 also batch 2 (config 4: one prompt, 4 Euler steps) and the CPU's batch-2 UNet call."""
+    ub = UNetBench(dist, device)
+    res = {"metric": "SD1.5 UNet denoise steps/s", "unit": "steps/s", "scaling": "strong",
+           "parallelism": f"batch-sharded x{dist.world} (prompts with both CFG halves local), latents all-gathered "
+                          "over NCCL every step",
+           "execution": "CUDA graph of one denoise step (channels-last activations); device time, max over ranks",
+           "model": "SD1.5-architecture UNet, random init (seeded), bf16",
+           "linear_layers_on_gemm_kernel": len(ub.rt.weights)}
+    for L in args.unet_latents:
+        res[f"batch16_{L}"] = ub.measure(16, L, args.steps, args.warmup, sampler=sampler)
+    if dist.world == 1:
+        res["batch2_64"] = ub.measure(2, 64, args.steps, args.warmup, sampler=sampler)
+        if dist.rank == 0 and not args.no_cpu:
+            res["cpu_baseline"] = ub.cpu_baseline(64)
+    return res
+
+
+def run_unet(args, dist) -> None:
+    """--workload unet: the UNet leg alone on one configuration, its own JSON line."""
+    device = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(device)
+    sampler = ClockSampler([_gpu_uuid(dist.local_rank)]) if dist.rank == 0 else None
+    if sampler is not None:
+        sampler.start()
+    ub = UNetBench(dist, device)
+    r = ub.measure(args.batch, args.latent, args.steps, args.warmup, args.unet_steps, sampler=sampler,
+                   kernel_times_out=args.kernel_times)
+    if sampler is not None:
+        sampler.stop()
+    kt = r.pop("kernel_times", None)
+    if kt is not None:
+        print(kt, file=sys.stderr, flush=True)
+    cpu = ub.cpu_baseline(args.latent) if (dist.rank == 0 and dist.world == 1 and not args.no_cpu) else None
     if dist.rank == 0:
-        line = {"metric": "SD1.5 UNet denoise steps/s", "value": round(1e3 / ms, 3), "unit": "steps/s",
-                "n_gpus": dist.world, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 3),
-                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic",
+        P = args.batch // 2
+        line = {"metric": "SD1.5 UNet denoise steps/s", "value": r["steps_per_s"], "unit": "steps/s",
+                "n_gpus": dist.world, "steps": args.steps, "warmup": max(3, args.warmup),
+                "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": f"sd15-unet-random-init batch {args.batch} ({P} prompts x CFG) "
                                        f"{args.latent}x{args.latent} latent, {args.unet_steps} Euler steps per image",
                            "parallelism": f"batch-sharded x{dist.world}, latents all-gathered per step",
-                           "s_per_image": round(ms * args.unet_steps / 1e3 / P, 5),
-                           "linear_layers_on_gemm_kernel": len(rt.weights)},
+                           "s_per_image": r["s_per_image"],
+                           "linear_layers_on_gemm_kernel": len(ub.rt.weights)},
                 "execution": "CUDA graph of one denoise step (channels-last activations)",
-                "cpu_baseline": cpu, "clocks": clocks}
+                "cpu_baseline": cpu, "clocks": r.get("clocks")}
         print(json.dumps(line), flush=True)
-    del g
 
 
 def run_case(args) -> None:
-    """--case: one kernel on one shape, `warmup` + `steps` launches (the small cases the ncu captures use)."""
+    """--case: one kernel on one shape, `warmup` + `steps` launches (the small cases the ncu summaries use)."""
     from npu_ai_b200 import kernels
     device = torch.device("cuda", 0)
     kind, dims = args.case.split(":")
@@ -796,16 +977,22 @@ def run_case(args) -> None:
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-unet", action="store_true", help="skip the UNet leg of the default run")
+    ap.add_argument("--unet-latents", default="64,128",
+                    help="latent sizes of the default run's batch-16 UNet leg (comma-separated)")
+    ap.add_argument("--soak-s", type=float, default=4.5,
+                    help="seconds of step replays right before the timed region (for the clock record)")
     ap.add_argument("--case", default=None, help="time one kernel: gemm:M,K,N, attn:B,H,Sq,Skv,D, geglu:M,K,n, "
                                                    "conv:n,h,w,cin,cout, gn:n,h,w,c, ln:rows,c, up:n,c,h,w or "
                                                    "cat:n,ca,cb,h,w")
     ap.add_argument("--workload", choices=["hotpath", "unet"], default="hotpath",
-                    help="hotpath: the GEMM sweep + attention blocks (default); unet: SD1.5 UNet denoise steps")
+                    help="hotpath: the driver's line (GEMM sweep + attention blocks, with the UNet leg); unet: only "
+                         "the UNet on one configuration")
     ap.add_argument("--batch", type=int, default=2, help="unet: images per step, both CFG halves (2 = 1 prompt)")
     ap.add_argument("--latent", type=int, default=64, help="unet: latent height/width")
     ap.add_argument("--unet-steps", type=int, default=4, help="unet: Euler steps per image")
@@ -814,6 +1001,7 @@ def main(argv=None) -> int:
                          "(torch profiler over three extra graph replays; the JSON line is unaffected)")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
+    args.unet_latents = [int(v) for v in str(args.unet_latents).split(",") if v.strip()]
     if args.case:
         run_case(args)
         return 0

@@ -156,11 +156,13 @@ int npub200_concat_channels(const void* a, int64_t lda, int64_t ca, const void* 
  * by its own pool manager and may not grow during a request, an FFI binding holding only the pointers it was
  * given, code that must not call cudaMalloc because it synchronises the device). No counterpart in the reference:
  * its NPU runner allocates its own pinned buffers. Same arguments and result as npub200_gemm minus the
- * workspace; the scratch is one fixed device array of NPUB200_NOALLOC_SCRATCH_BYTES per GPU, held from library
- * load to process exit, and this call allocates nothing. A shape whose scratch need exceeds the array is rejected
- * with NPUB200_EINVAL. The first call on a device resolves the array and clears its leading region (make it before
- * any stream capture). All calls share the array and it keeps the last call's contents: calls that overlap on the GPU
- * (several streams, several host threads) race and must be serialised by the caller, e.g. on one stream.
+ * workspace. The only scratch such a GEMM needs is a repacked copy of an operand TMA cannot address (K % 8 != 0,
+ * a row stride that is not a multiple of 8 elements, an unaligned base); here it goes to one fixed device array of
+ * NPUB200_NOALLOC_SCRATCH_BYTES per GPU, held from library load to process exit, and this call allocates nothing.
+ * A shape whose repacked operands (plus a reserved 4 KiB) exceed the array is rejected with NPUB200_EINVAL;
+ * npub200_gemm_workspace_size gives that need. The first call on a device resolves the array's address (make it
+ * before any stream capture). All calls share the array and it keeps the last call's contents: calls that overlap
+ * on the GPU (several streams, several host threads) race and must be serialised by the caller, e.g. on one stream.
  * ---------------------------------------------------------------------------------------------------------- */
 #define NPUB200_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
 int npub200_gemm_noalloc(const void* x, int64_t ldx, int64_t m, int64_t k, const void* w, int64_t ldw, int64_t n,

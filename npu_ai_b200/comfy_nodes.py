@@ -21,6 +21,7 @@ import threading
 import time
 import types
 import weakref
+from dataclasses import dataclass, field
 
 import numpy as np
 import torch
@@ -47,61 +48,79 @@ def _mode(m: str) -> str:
     return {"npu": "gpu", "cpu": "off"}.get(m, m if m in ATTENTION_MODES else "auto")
 
 
-class AttentionGate:
-    """Per-shape choice of the fused-attention kernel variant (the reference's AttentionGate, node :39-99).
+@dataclass
+class ShapeRecord:
+    """The gate's knowledge of one attention shape, keyed (batch, query tokens, key tokens, heads, head dim)."""
+    variant_ms: dict[int, float] = field(default_factory=dict)  # timed once per variant on the first call
+    model_ms: float | None = None        # the model's own attention, timed after one warm-up call
+    variant: int | None = None           # the fused-kernel variant this shape runs
+    model_reason: str | None = None      # set when the shape must run the model's own attention
+    max_rel_err: float | None = None     # first-call check against the model's own attention
 
-    ``auto``: every variant is timed once per shape on the first call (CUDA events) and the fastest is kept;
-    ``gpu``: the default variant; ``off``: the model's own attention. Masked / GQA calls and calls with fewer than
-    ``min_tokens`` query rows use the model's own attention in every mode, logged once with the reason.
+    def describe(self) -> str:
+        parts = [f"variant {v} {t:.3f} ms" for v, t in sorted(self.variant_ms.items())]
+        if self.model_ms is not None:
+            parts.append(f"model {self.model_ms:.3f} ms")
+        if self.max_rel_err is not None:
+            parts.append(f"max rel err {self.max_rel_err:.1e}")
+        outcome = self.model_reason if self.model_reason is not None else \
+            ("pending" if self.variant is None else f"variant {self.variant}")
+        return ", ".join(parts) + f" -> {outcome}"
+
+
+class AttentionGate:
+    """Which fused-attention variant each attention shape runs (the role of the reference's AttentionGate,
+    node :39-99; there the choice is NPU or CPU, here it is among kernel variants only).
+
+    Mode ``auto`` times every variant the head dim allows once, on the shape's first call, and keeps the fastest;
+    ``gpu`` keeps the kernel's own automatic variant; ``off`` (the reference's ``cpu``) hands every call to the
+    model's own attention. In every mode the first fused result of a shape is compared with the model's own
+    attention (max relative error <= 0.1, else RuntimeError). The model's attention also serves the calls the
+    kernel does not implement: an attention mask or grouped-query heads. ``min_tokens`` (default 1, so every SD1.5
+    self- and cross-attention, the 64-token middle block included, stays on the kernel) sends shorter query
+    sequences there too; each such shape is logged once with its reason.
     """
 
-    def __init__(self):
-        self.mode = "auto"
-        self.min_tokens = 256
-        self.ms: dict[tuple, dict[int, float]] = {}
-        self.ref_ms: dict[tuple, float] = {}
-        self.decision: dict[tuple, int | str] = {}
-        self.reason: dict[tuple, str] = {}
-        self.max_err: dict[tuple, float] = {}
-        self.counts = {"gpu": 0, "model": 0}
-        self.gpu_seconds = 0.0
+    def __init__(self, mode: str = "auto", min_tokens: int = 1):
+        self.mode = mode
+        self.min_tokens = min_tokens
+        self.shapes: dict[tuple, ShapeRecord] = {}
+        self.fused_calls = 0
+        self.model_calls = 0
+        self.fused_seconds = 0.0     # host time of the calls (kernel launches are asynchronous)
         self.model_seconds = 0.0
-        self.flops_gpu = 0.0
+        self.fused_flops = 0.0
 
-    def decide_static(self, key, mask, enable_gqa, fits) -> str | None:
-        reason = None
-        if self.mode == "off":
-            reason = "attention mode = off"
-        elif mask is not None:
-            reason = "masked attention"
-        elif enable_gqa:
-            reason = "grouped-query attention"
-        elif not fits:
-            reason = "outside the fused kernel's range"
-        elif key[1] < self.min_tokens:
-            reason = f"fewer than {self.min_tokens} query tokens"
-        if reason is None:
-            return None
-        if key not in self.reason:
-            self.reason[key] = reason
-            _log(f"attention {key} uses the model's own attention: {reason}")
-        return "model"
+    def record(self, key: tuple) -> ShapeRecord:
+        rec = self.shapes.get(key)
+        if rec is None:
+            rec = self.shapes[key] = ShapeRecord()
+        return rec
+
+    def model_route_reason(self, key: tuple, masked: bool, gqa: bool, fits: bool) -> str | None:
+        """Why this call must run the model's own attention, or None when the fused kernel takes it."""
+        rules = ((self.mode == "off", "attention mode = off"),
+                 (masked, "masked attention"),
+                 (gqa, "grouped-query attention"),
+                 (not fits, "outside the fused kernel's range"),
+                 (key[1] < self.min_tokens, f"fewer than {self.min_tokens} query tokens"))
+        why = next((text for hit, text in rules if hit), None)
+        if why is not None:
+            rec = self.record(key)
+            if rec.model_reason is None:
+                rec.model_reason = why
+                _log(f"attention {key} runs the model's own attention: {why}")
+        return why
+
+    def reset(self) -> None:
+        self.shapes.clear()
 
     def table(self) -> str:
-        rows = []
-        for key in sorted(set(self.ms) | set(self.reason)):
-            d = self.decision.get(key, self.reason.get(key, "pending"))
-            row = f"{key}: " + ", ".join(f"variant {v} {t:.3f} ms" for v, t in sorted(self.ms.get(key, {}).items()))
-            if key in self.ref_ms:
-                row += f", model {self.ref_ms[key]:.3f} ms"
-            if key in self.max_err:
-                row += f", max rel err {self.max_err[key]:.1e}"
-            rows.append(row + f" -> {d}")
-        return "; ".join(rows)
+        return "; ".join(f"{key}: {rec.describe()}" for key, rec in sorted(self.shapes.items()))
 
     def summary(self) -> str:
-        return (f"attention: {self.counts['gpu']} calls on the fused kernel ({self.gpu_seconds:.2f}s), "
-                f"{self.counts['model']} on the model's own attention ({self.model_seconds:.2f}s); "
+        return (f"attention: {self.fused_calls} calls on the fused kernel ({self.fused_seconds:.2f}s), "
+                f"{self.model_calls} on the model's own attention ({self.model_seconds:.2f}s); "
                 f"gate: {self.table()}")
 
 
@@ -115,14 +134,26 @@ def _time_gpu(fn, device) -> tuple[object, float]:
 
 
 class B200Runtime:
-    """Process-wide GPU runtime plus the Linear modules it has taken over (the reference's XDNA1Runtime,
-    node :102-143)."""
+    """The process-wide GPU side of the nodes: the runner, the gate, and every module whose forward it replaced
+    (the role of the reference's XDNA1Runtime, node :102-143, with a resident [N, K] weight per Linear instead of a
+    transposed NPU upload)."""
 
     def __init__(self, device=None):
         from .runner import NpuGemm  # loads libnpub200.so; fails loudly without it
         self.gemm = NpuGemm(device=device, verbose=False)
-        self.weights: dict[int, tuple] = {}      # id(module) -> (NpuWeight, bias tensor | None, name)
-        self.installed: dict[int, tuple] = {}    # id(module) -> (module, original forward)
+        self.attn = AttentionGate()
+        # Switches the node's UNet wrapper flips around each call: `enabled` routes patched modules to the kernels;
+        # `record_only` (the shape-discovery pass) runs them on torch and collects each GEMM's (tokens, K, N).
+        self.enabled = False
+        self.record_only = False
+        self.recorded: set[tuple[int, int, int]] = set()
+        self.min_tokens = 64          # Linear calls with fewer rows keep torch's F.linear
+        self.calls = 0
+        self.last_summary = ""
+        # Every patched module: patched[id] = (module, the forward it had before), restored by release().
+        self.patched: dict[int, tuple] = {}
+        # Linears on the GEMM kernel: weights[id] = (resident NpuWeight, f32 bias on the device or None, name).
+        self.weights: dict[int, tuple] = {}
         self.geglu_modules: set[int] = set()     # GEGLU modules routed to the fused projection + gating kernel
         # Sibling projections fed the same input (self-attention q/k/v, cross-attention k/v) run as ONE GEMM over
         # the concatenated weight: leader id -> (fused NpuWeight, fused bias | None, [(member id, column slice)]),
@@ -158,37 +189,40 @@ class B200Runtime:
         self.norm_silu: dict[int, tuple] = {}
         # A second stream per device for work off a ResBlock's critical path (its 1x1 skip convolution).
         self.side_streams: dict[int, torch.cuda.Stream] = {}
-        self.enabled = False
-        self.record_only = False
-        self.recorded: set[tuple[int, int, int]] = set()
-        self.min_tokens = 64
-        self.calls = 0
-        self.last_summary = ""
-        self.attn = AttentionGate()
+
+    def _patch(self, mod: torch.nn.Module, forward) -> None:
+        """Swap `mod.forward` for `forward` bound to it, keeping the old one for release()."""
+        self.patched[id(mod)] = (mod, mod.forward)
+        mod.forward = types.MethodType(forward, mod)
+
+    @staticmethod
+    def _linear_eligible(name: str, mod: torch.nn.Module, min_features: int, skip: tuple[str, ...]) -> bool:
+        """A Linear the node takes over: both feature counts reach `min_features` and no `skip` substring occurs
+        in its module name (the reference's filter, node :119-136)."""
+        if not isinstance(mod, torch.nn.Linear):
+            return False
+        if min(mod.in_features, mod.out_features) < min_features:
+            return False
+        return not any(s and s in name for s in skip)
 
     def take_over(self, diffusion_model: torch.nn.Module, min_features: int, skip: tuple[str, ...],
                   convolutions: bool = True) -> int:
-        n_new = 0
-        for name, mod in diffusion_model.named_modules():
-            if not isinstance(mod, torch.nn.Linear) or id(mod) in self.installed:
-                continue
-            if any(s and s in name for s in skip):
-                continue
-            if mod.in_features < min_features or mod.out_features < min_features:
-                continue
-            w = self.gemm.upload_weight(mod.weight.detach(), layout="nk")   # nn.Linear's [N, K]: no transpose
-            bias = mod.bias.detach().to(self.gemm.device, torch.float32).contiguous() if mod.bias is not None else None
-            self.weights[id(mod)] = (w, bias, name)
-            self.installed[id(mod)] = (mod, mod.forward)
-            mod.forward = types.MethodType(_gpu_linear_forward, mod)
-            n_new += 1
+        """Patch the model's eligible modules onto the kernels; returns how many Linears were newly taken."""
+        todo = [(name, mod) for name, mod in diffusion_model.named_modules()
+                if id(mod) not in self.patched and self._linear_eligible(name, mod, min_features, skip)]
+        dev = self.gemm.device
+        for name, lin in todo:
+            bias = None if lin.bias is None else lin.bias.detach().to(dev, torch.float32).contiguous()
+            # nn.Linear's own [N, K] weight is the kernel's B operand: no transpose
+            self.weights[id(lin)] = (self.gemm.upload_weight(lin.weight.detach(), layout="nk"), bias, name)
+            self._patch(lin, _gpu_linear_forward)
+        n_new = len(todo)
         self._fuse_projections(diffusion_model)
         for mod in diffusion_model.modules():
             plan = _tblock_plan(mod, self)
-            if plan is not None and id(mod) not in self.installed:
+            if plan is not None and id(mod) not in self.patched:
                 self.tblocks[id(mod)] = plan
-                self.installed[id(mod)] = (mod, mod.forward)
-                mod.forward = types.MethodType(_gpu_tblock_forward, mod)
+                self._patch(mod, _gpu_tblock_forward)
         for mod in diffusion_model.modules():
             if id(mod) not in self.tblocks:
                 continue
@@ -196,21 +230,19 @@ class B200Runtime:
                 ln = getattr(mod, nm, None)
                 if (isinstance(ln, torch.nn.LayerNorm) and ln.elementwise_affine and ln.bias is not None
                         and len(ln.normalized_shape) == 1 and ln.normalized_shape[0] % 8 == 0
-                        and ln.normalized_shape[0] <= 2048 and id(ln) not in self.installed):
+                        and ln.normalized_shape[0] <= 2048 and id(ln) not in self.patched):
                     self.lnorms[id(ln)] = (ln.weight.detach().to(self.gemm.device, torch.float32).contiguous(),
                                            ln.bias.detach().to(self.gemm.device, torch.float32).contiguous())
-                    self.installed[id(ln)] = (ln, ln.forward)
-                    ln.forward = types.MethodType(_gpu_layer_norm_forward, ln)
+                    self._patch(ln, _gpu_layer_norm_forward)
         if convolutions:
             self._take_over_convs(diffusion_model)
         # GEGLU feed-forward blocks whose projection was taken over: projection + gating in one kernel.
         for name, mod in diffusion_model.named_modules():
             proj = getattr(mod, "proj", None)
             if (type(mod).__name__ == "GEGLU" and isinstance(proj, torch.nn.Linear) and id(proj) in self.weights
-                    and id(mod) not in self.installed and proj.out_features % 2 == 0):
-                self.installed[id(mod)] = (mod, mod.forward)
+                    and id(mod) not in self.patched and proj.out_features % 2 == 0):
                 self.geglu_modules.add(id(mod))
-                mod.forward = types.MethodType(_gpu_geglu_forward, mod)
+                self._patch(mod, _gpu_geglu_forward)
         return n_new
 
     def _fuse_projections(self, diffusion_model: torch.nn.Module) -> None:
@@ -242,7 +274,7 @@ class B200Runtime:
         from . import kernels
         dev = self.gemm.device
         for mod in dm.modules():
-            if id(mod) in self.installed:
+            if id(mod) in self.patched:
                 continue
             if isinstance(mod, torch.nn.Conv2d) and mod.groups == 1 and mod.dilation == (1, 1) \
                     and mod.padding_mode == "zeros":
@@ -257,40 +289,34 @@ class B200Runtime:
                 else:
                     continue
                 self.convs[id(mod)] = entry
-                self.installed[id(mod)] = (mod, mod.forward)
-                mod.forward = types.MethodType(_gpu_conv_forward, mod)
+                self._patch(mod, _gpu_conv_forward)
             elif isinstance(mod, torch.nn.GroupNorm) and mod.affine and mod.num_channels % 8 == 0:
                 self.norms[id(mod)] = (mod.weight.detach().to(dev, torch.float32).contiguous(),
                                        mod.bias.detach().to(dev, torch.float32).contiguous())
-                self.installed[id(mod)] = (mod, mod.forward)
-                mod.forward = types.MethodType(_gpu_group_norm_forward, mod)
+                self._patch(mod, _gpu_group_norm_forward)
         for mod in dm.modules():
             plan = _resblock_plan(mod, self)
-            if plan is not None and id(mod) not in self.installed:
+            if plan is not None and id(mod) not in self.patched:
                 self.resblocks[id(mod)] = plan
-                self.installed[id(mod)] = (mod, mod.forward)
-                mod.forward = types.MethodType(_gpu_resblock_forward, mod)
+                self._patch(mod, _gpu_resblock_forward)
         for mod in dm.modules():
-            if id(mod) in self.installed:
+            if id(mod) in self.patched:
                 continue
             if (type(mod).__name__ == "Upsample" and getattr(mod, "dims", 2) == 2 and getattr(mod, "use_conv", True)
                     and self.convs.get(id(getattr(mod, "conv", None)), ("",))[0] == "3x3"):
                 self.upsamples.add(id(mod))
-                self.installed[id(mod)] = (mod, mod.forward)
-                mod.forward = types.MethodType(_gpu_upsample_forward, mod)
+                self._patch(mod, _gpu_upsample_forward)
                 continue
             plan = _stransformer_plan(mod, self)
             if plan is not None:
                 self.stransformers[id(mod)] = plan
-                self.installed[id(mod)] = (mod, mod.forward)
-                mod.forward = types.MethodType(_gpu_spatial_transformer_forward, mod)
+                self._patch(mod, _gpu_spatial_transformer_forward)
                 continue
             if (type(mod) is torch.nn.Sequential and len(mod) == 3 and isinstance(mod[0], torch.nn.GroupNorm)
                     and id(mod[0]) in self.norms and isinstance(mod[1], torch.nn.SiLU)
                     and isinstance(mod[2], torch.nn.Conv2d)):
                 self.norm_silu[id(mod)] = (mod[0], mod[2])
-                self.installed[id(mod)] = (mod, mod.forward)
-                mod.forward = types.MethodType(_gpu_norm_silu_conv_forward, mod)
+                self._patch(mod, _gpu_norm_silu_conv_forward)
         by_width: dict[int, list] = {}
         for mod in dm.modules():
             if id(mod) in self.resblocks and id(mod) not in self.emb_slices:
@@ -335,7 +361,7 @@ class B200Runtime:
         return st
 
     def release(self) -> None:
-        for mod, orig in self.installed.values():
+        for mod, orig in self.patched.values():
             mod.forward = orig
         for w, _, _ in self.weights.values():
             w.release()
@@ -361,7 +387,7 @@ class B200Runtime:
         self.fused_groups.clear()
         self.fused_member.clear()
         self.pending.clear()
-        self.installed.clear()
+        self.patched.clear()
         self.weights.clear()
         self.geglu_modules.clear()
         self.enabled = False
@@ -412,9 +438,9 @@ def _gpu_geglu_forward(self, x: torch.Tensor) -> torch.Tensor:
     entry = rt.weights.get(id(proj)) if rt is not None else None
     tokens = x.numel() // x.shape[-1] if x.numel() else 0
     if (entry is None or not rt.enabled or rt.record_only or tokens < rt.min_tokens or x.device.type != "cuda"
-            or id(self) not in rt.installed):
-        if rt is not None and id(self) in rt.installed:
-            return rt.installed[id(self)][1](x)
+            or id(self) not in rt.patched):
+        if rt is not None and id(self) in rt.patched:
+            return rt.patched[id(self)][1](x)
         a, gate = proj(x).chunk(2, dim=-1)
         return a * torch.nn.functional.gelu(gate)
     w, bias, _name = entry
@@ -472,7 +498,7 @@ def _gpu_tblock_forward(self, x, context=None, transformer_options=None, **kwarg
     if (plan is None or not _runtime_on(rt) or kwargs or self.training or not x.is_cuda or x.dtype != torch.bfloat16
             or not x.is_contiguous() or to.get("patches") or to.get("patches_replace")
             or getattr(self, "disable_self_attn", False)):
-        return rt.installed[id(self)][1](x, context, transformer_options, **kwargs)
+        return rt.patched[id(self)][1](x, context, transformer_options, **kwargs)
     o1, o2, o3 = plan
     x = _with_residual(rt, o1, x, lambda: self.attn1(self.norm1(x), context=None, transformer_options=to))
     x = _with_residual(rt, o2, x, lambda: self.attn2(self.norm2(x), context=context, transformer_options=to))
@@ -505,7 +531,7 @@ def _gpu_conv_forward(self, x: torch.Tensor) -> torch.Tensor:
     entry = rt.convs.get(id(self)) if rt is not None else None
     n, c, h, w = x.shape if x.dim() == 4 else (0, 0, 0, 0)
     if entry is None or not _runtime_on(rt) or not _cl_bf16(x) or (entry[0] == "3x3" and not _conv_tiles(h, w)):
-        return rt.installed[id(self)][1](x) if rt is not None and id(self) in rt.installed else \
+        return rt.patched[id(self)][1](x) if rt is not None and id(self) in rt.patched else \
             torch.nn.Conv2d.forward(self, x)
     from . import kernels
     rt.conv_calls += 1
@@ -527,8 +553,8 @@ def _gpu_conv_forward(self, x: torch.Tensor) -> torch.Tensor:
 
 def _own_forward(rt, mod):
     """The forward a module had before the takeover (its class's forward once the runtime is gone)."""
-    if rt is not None and id(mod) in rt.installed:
-        return rt.installed[id(mod)][1]
+    if rt is not None and id(mod) in rt.patched:
+        return rt.patched[id(mod)][1]
     return types.MethodType(type(mod).forward, mod)
 
 
@@ -618,7 +644,7 @@ def _gpu_group_norm_forward(self, x: torch.Tensor) -> torch.Tensor:
     rt = _RUNTIME
     entry = rt.norms.get(id(self)) if rt is not None else None
     if entry is None or not _runtime_on(rt) or not _cl_bf16(x):
-        return rt.installed[id(self)][1](x) if rt is not None and id(self) in rt.installed else \
+        return rt.patched[id(self)][1](x) if rt is not None and id(self) in rt.patched else \
             torch.nn.GroupNorm.forward(self, x)
     from . import kernels
     out = torch.empty_like(x, memory_format=torch.channels_last)
@@ -634,7 +660,7 @@ def _gpu_layer_norm_forward(self, x: torch.Tensor) -> torch.Tensor:
     entry = rt.lnorms.get(id(self)) if rt is not None else None
     if (entry is None or not _runtime_on(rt) or not isinstance(x, torch.Tensor) or not x.is_cuda
             or x.dtype != torch.bfloat16 or not x.is_contiguous() or x.shape[-1] != entry[0].shape[0]):
-        return rt.installed[id(self)][1](x) if rt is not None and id(self) in rt.installed else \
+        return rt.patched[id(self)][1](x) if rt is not None and id(self) in rt.patched else \
             torch.nn.LayerNorm.forward(self, x)
     from . import kernels
     return kernels.layer_norm(x, entry[0], entry[1], eps=self.eps)
@@ -704,7 +730,7 @@ def _gpu_resblock_forward(self, x, emb, *args, **kwargs):
     plan = rt.resblocks.get(id(self)) if rt is not None else None
     if plan is None or not _runtime_on(rt) or not _cl_bf16(x) or self.training or args or \
             any(k != "transformer_options" for k in kwargs) or not _conv_tiles(x.shape[2], x.shape[3]):
-        return rt.installed[id(self)][1](x, emb, *args, **kwargs)
+        return rt.patched[id(self)][1](x, emb, *args, **kwargs)
     from . import kernels
     rt.conv_calls += 1
     gn1, conv1, gn2, conv2, skip = plan
@@ -763,11 +789,12 @@ def _gpu_attention_override(func, q, k, v, heads, mask=None, attn_precision=None
         tk = k.shape[1]
     key = (b, tq, tk, h, d)
     fits = rt.gemm.attention_fits(tq, tk, d, b * h)
-    if gate.decide_static(key, mask, kwargs.get("enable_gqa", False), fits) == "model" or rt.record_only:
+    why = gate.model_route_reason(key, mask is not None, bool(kwargs.get("enable_gqa", False)), fits)
+    if why is not None or rt.record_only:
         t0 = time.perf_counter()
         out = model_attn()
         gate.model_seconds += time.perf_counter() - t0
-        gate.counts["model"] += 1
+        gate.model_calls += 1
         return out
     scale = kwargs.get("scale", None)
     out_dtype = q.dtype if q.dtype in (torch.bfloat16, torch.float32) else torch.float32
@@ -778,33 +805,29 @@ def _gpu_attention_override(func, q, k, v, heads, mask=None, attn_precision=None
         return kernels.attention(qd, kd, vd, h, scale=scale, head_major_in=skip_reshape,
                                  head_major_out=skip_output_reshape, out_dtype=out_dtype, variant=variant)
 
-    decision = gate.decision.get(key)
-    if decision is None:
-        # First call of this shape: time the variants, check against the model's own attention once.
-        variants = attn_variants(d) if gate.mode == "auto" else (0,)
+    rec = gate.record(key)
+    if rec.variant is None:
+        # First call of this shape: time the variants (each after one warm-up launch), then check the first
+        # result against the model's own attention, also timed after a warm-up call.
         y = None
-        for var in variants:
-            fused(var)  # warm-up
-            y_v, ms = _time_gpu(lambda: fused(var), rt.gemm.device)
-            gate.ms.setdefault(key, {})[var] = ms
-            if y is None:
-                y = y_v
-        ref, ref_ms = _time_gpu(model_attn, rt.gemm.device)
-        gate.ref_ms[key] = ref_ms
+        for var in (attn_variants(d) if gate.mode == "auto" else (0,)):
+            fused(var)
+            y_v, rec.variant_ms[var] = _time_gpu(lambda: fused(var), rt.gemm.device)
+            y = y_v if y is None else y
+        model_attn()
+        ref, rec.model_ms = _time_gpu(model_attn, rt.gemm.device)
         err = float((y.float() - ref.float()).abs().max() / (ref.float().abs().max() + 1e-12))
-        gate.max_err[key] = err
+        rec.max_rel_err = err
         if not np.isfinite(err) or err > 0.1:
             raise RuntimeError(f"fused attention result for {key} does not match the model's attention "
                                f"(max rel err {err:.3g})")
-        decision = min(gate.ms[key], key=gate.ms[key].get)
-        gate.decision[key] = decision
-        _log(f"attention gate {key}: " + ", ".join(f"variant {v} {t:.3f} ms" for v, t in sorted(gate.ms[key].items()))
-             + f" (model's own {ref_ms:.3f} ms), max rel err {err:.1e} -> variant {decision}")
+        rec.variant = min(rec.variant_ms, key=rec.variant_ms.get)
+        _log(f"attention gate {key}: {rec.describe()}")
     t0 = time.perf_counter()
-    y = fused(decision)
-    gate.gpu_seconds += time.perf_counter() - t0
-    gate.counts["gpu"] += 1
-    gate.flops_gpu += 4.0 * b * h * tq * tk * d
+    y = fused(rec.variant)
+    gate.fused_seconds += time.perf_counter() - t0
+    gate.fused_calls += 1
+    gate.fused_flops += 4.0 * b * h * tq * tk * d
     return y
 
 
@@ -837,9 +860,10 @@ class B200LinearOffload:
                                                 "tooltip": "auto = time the fused kernel's variants per shape once "
                                                            "and keep the fastest, gpu = default variant, off = the "
                                                            "model's own attention"}),
-                "attn_min_tokens": ("INT", {"default": 256, "min": 1, "max": 65536,
+                "attn_min_tokens": ("INT", {"default": 1, "min": 1, "max": 65536,
                                             "tooltip": "attention calls with fewer query tokens use the model's "
-                                                       "own attention"}),
+                                                       "own attention (1: every unmasked call runs the fused "
+                                                       "kernel)"}),
                 "convolutions": ("BOOLEAN", {"default": True,
                                              "tooltip": "also run 3x3/1x1 convolutions, GroupNorms and ResBlocks "
                                                         "of channels-last bf16 models on the B200 kernels"}),
@@ -851,7 +875,7 @@ class B200LinearOffload:
     CATEGORY = "GPU/B200"
     DESCRIPTION = "Runs the model's Linear layers and attention on hand-written B200 (sm_100a) kernels."
 
-    def apply(self, model, enabled, min_tokens, min_features, skip_names, attention="auto", attn_min_tokens=256,
+    def apply(self, model, enabled, min_tokens, min_features, skip_names, attention="auto", attn_min_tokens=1,
               convolutions=True):
         if not enabled:
             return (model,)
@@ -859,8 +883,7 @@ class B200LinearOffload:
         rt.min_tokens = int(min_tokens)
         mode = _mode(attention)
         if mode != rt.attn.mode or int(attn_min_tokens) != rt.attn.min_tokens:
-            rt.attn.decision.clear()
-            rt.attn.reason.clear()
+            rt.attn.reset()
             _log(f"attention mode {rt.attn.mode} -> {mode} (min tokens {attn_min_tokens}); gate decisions reset")
         rt.attn.mode = mode
         rt.attn.min_tokens = int(attn_min_tokens)
@@ -870,8 +893,8 @@ class B200LinearOffload:
         def snapshot():
             rt.gemm.flush_timing()
             g, a = rt.gemm.stats, rt.attn
-            return dict(g, attn_gpu=a.counts["gpu"], attn_model=a.counts["model"], attn_gpu_s=a.gpu_seconds,
-                        attn_model_s=a.model_seconds, attn_flops=a.flops_gpu)
+            return dict(g, attn_gpu=a.fused_calls, attn_model=a.model_calls, attn_gpu_s=a.fused_seconds,
+                        attn_model_s=a.model_seconds, attn_flops=a.fused_flops)
 
         def wrapper(apply_model, args):
             x, t, c = args["input"], args["timestep"], args["c"]

@@ -497,8 +497,6 @@ int npub200_status_read(void* stream, uint32_t* bits_out, int clear) {
   if (clear && bits) {
     const uint32_t zero = 0;
     if (int rc = check_cuda(cudaMemcpyToSymbol(g_status_word, &zero, sizeof(zero)), "clear status word")) return rc;
-    if (int rc = noalloc_reset_counters(d->device, st)) return rc;
-    if (int rc = check_cuda(cudaStreamSynchronize(st), "cudaStreamSynchronize")) return rc;
   }
   if (bits_out) *bits_out = bits;
   return kOk;

@@ -1,19 +1,24 @@
 // gemm_noalloc.cu - the GEMM entry point for callers that cannot allocate device memory.
 //
-// npub200_gemm needs a caller-provided workspace for its split-K partials (and for repacking operands TMA cannot
-// address). Some callers have no way to provide one: a host application whose device memory belongs to its own
-// pool manager and that forbids allocations while it serves a request, an FFI binding that holds only the
-// pointers it was handed (no allocator of its own), or code that must not call cudaMalloc because that call
-// synchronises the whole device mid-stream. npub200_gemm_noalloc serves them: the scratch lives in one file-scope
-// device array of a fixed size that every GPU loading this library keeps until process exit; the entry point
-// itself calls no cudaMalloc, cudaFree or allocating library routine.
+// npub200_gemm needs a caller-provided workspace when an operand is not TMA-addressable (K % 8 != 0, a row stride
+// that is not a multiple of 8 elements, an unaligned base): the kernel reads a repacked dense copy of it. Some
+// callers have no way to provide one: a host application whose device memory belongs to its own pool manager and
+// that forbids allocations while it serves a request, an FFI binding that holds only the pointers it was handed (no
+// allocator of its own), or code that must not call cudaMalloc because that call synchronises the whole device
+// mid-stream. npub200_gemm_noalloc serves them: the repacked operands go to one file-scope device array of a fixed
+// size that every GPU loading this library keeps until process exit; the entry point itself calls no cudaMalloc,
+// cudaFree or allocating library routine.
 //
-// Sharing rules: every call on a device uses the same array, and the array keeps the last call's contents (the
-// operands a call had to repack; split K reduces inside a cluster and leaves nothing there). The first call on
-// each device resolves the array's address and clears its leading 64 KiB once, synchronising its stream, so that
-// first call must not be inside a stream capture. Calls whose work overlaps on the GPU (different streams, or host
-// threads racing on one device) race on the array: callers must serialise them, e.g. by issuing every call on one
-// stream.
+// What the array holds: after a 4 KiB leading region that the workspace layout reserves (nothing reads or writes
+// it), the repacked x and/or W of the latest call that needed them. Split K needs no scratch (its partials are
+// reduced in a cluster's distributed shared memory). Every repack writes all the bytes the kernel then reads, pad
+// columns included, so nothing has to start at zero and nothing is cleared.
+//
+// Sharing rules: every call on a device uses the same array, and the array keeps the last call's contents. The
+// first call on each device resolves the array's device address (cudaGetSymbolAddress, which may load the module's
+// device code), so make that first call before any stream capture. Calls whose work overlaps on the GPU (different
+// streams, or host threads racing on one device) race on the array: callers must serialise them, e.g. by issuing
+// every call on one stream.
 #include <cstring>
 #include <mutex>
 
@@ -22,24 +27,25 @@
 
 namespace npub200 {
 
-// The shared scratch (repacked operands, after a reserved leading region). Host code sees only a stand-in for this
+// The shared scratch (repacked operands, after the reserved leading region). Host code sees only a stand-in for this
 // symbol; its device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NPUB200_NOALLOC_SCRATCH_BYTES];
 
 namespace {
 
+constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
-void* g_scratch_ptr[64] = {nullptr};
+void* g_scratch_ptr[kMaxDevices] = {nullptr};
 
-// Once per device, with that device current: resolve the array's device address and clear its leading region.
-int noalloc_setup(int device, cudaStream_t stream, void** out) {
+// Once per device, with that device current: resolve the array's device address (no allocation, no device sync).
+int noalloc_setup(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices)
+    return fail(kErrInvalid, "npub200_gemm_noalloc: device ordinal %d outside [0, %d)", device, kMaxDevices);
   std::lock_guard<std::mutex> lock(g_setup_mutex);
   if (g_scratch_ptr[device] == nullptr) {
     void* p = nullptr;
     if (int rc = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)"))
       return rc;
-    if (int rc = check_cuda(cudaMemsetAsync(p, 0, 65536, stream), "clear no-alloc scratch")) return rc;
-    if (int rc = check_cuda(cudaStreamSynchronize(stream), "clear no-alloc scratch (sync)")) return rc;
     g_scratch_ptr[device] = p;
   }
   *out = g_scratch_ptr[device];
@@ -47,14 +53,6 @@ int noalloc_setup(int device, cudaStream_t stream, void** out) {
 }
 
 }  // namespace
-
-// After a kernel reported a failure: clear the leading region again (no-op when the array was never used on this
-// device).
-int noalloc_reset_counters(int device, cudaStream_t stream) {
-  std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (device < 0 || device >= 64 || g_scratch_ptr[device] == nullptr) return kOk;
-  return check_cuda(cudaMemsetAsync(g_scratch_ptr[device], 0, 65536, stream), "clear no-alloc scratch");
-}
 
 }  // namespace npub200
 
@@ -75,7 +73,7 @@ extern "C" int npub200_gemm_noalloc(const void* x, int64_t ldx, int64_t m, int64
                 "library's fixed %d-byte array; use npub200_gemm with a workspace",
                 (long long)m, (long long)k, (long long)n, need, int(NPUB200_NOALLOC_SCRATCH_BYTES));
   void* scratch = nullptr;
-  if (int rc = noalloc_setup(dev->device, static_cast<cudaStream_t>(stream), &scratch)) return rc;
+  if (int rc = noalloc_setup(dev->device, &scratch)) return rc;
   return gemm_with_workspace(x, ldx, m, k, w, ldw, n, nullptr, bias, bias_dtype, out, ldo, out_dtype, scratch,
                              size_t(NPUB200_NOALLOC_SCRATCH_BYTES), variant, stream);
 }

@@ -5,11 +5,12 @@
 // `gemm_step`/`gemm_zero`/`gemm_store`). Same arithmetic contract: bf16 operands, f32 accumulation, bias added
 // in f32 after the accumulation (xdna1_gemm.py:417-418); the output is f32 (the reference's) or bf16.
 //
-// Design (one persistent CTA per SM, 192 threads):
+// Design (one persistent CTA per SM, 320 threads = kGemmThreads):
 //   warp 0      TMA producer: 128x64 tiles of x and BNx64 tiles of W (128-byte swizzle) into a STAGES-deep ring
 //   warp 1      TMEM owner + MMA issuer: tcgen05.mma kind::f16, M=128, N=BN, K=16 steps, f32 accumulators in
 //               TMEM, double-buffered so the epilogue of tile i overlaps the main loop of tile i+1
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator rows, bias add, cast, predicated stores
+//   warps 2-9   epilogue, two warps per TMEM lane quarter on alternate 64-column chunks: tcgen05.ld of the
+//               accumulator rows, bias add, cast, swizzled staging + TMA store (or predicated direct stores)
 // Ragged M/N/K need no padding: TMA zero-fills out-of-bounds rows and columns, the epilogue stores only rows < M
 // and columns < N.
 // GEGLU form (template flag): W holds 2N rows ([a; gate], the GEGLU projection of SD1.5's feed-forward block) and
@@ -26,6 +27,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "internal.h"
 
@@ -912,10 +914,13 @@ bool gemm_variant_known(int variant, bool geglu) {
 }
 
 int gemm_cluster_slots(int size) {
+  // Filled once per (device, cluster size) under a lock: planning runs on any host thread.
+  static std::mutex fill_mutex;
   static int slots[64][kGemmMaxSplits + 1] = {};
   if (size < 2 || size > kGemmMaxSplits) return 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(fill_mutex);
   if (slots[dev][size] == 0) {
     // Every GEMM instantiation holds one CTA per SM (more than half of the shared memory), so one stands for all.
     using L = GemmLayout<64, 8>;

@@ -158,9 +158,6 @@ size_t conv3x3_workspace_bytes(int64_t n, int64_t h, int64_t w, int64_t cin, int
 int repack_rows_bf16(const void* src, int64_t ld_src, int64_t rows, int64_t cols, void* dst, int64_t cols_pad,
                      cudaStream_t stream);
 
-// Clears the no-allocation entry point's split-K counters on `device` (after a kernel reported a failure).
-int noalloc_reset_counters(int device, cudaStream_t stream);
-
 // ---- attention ---------------------------------------------------------------------------------------------------
 struct AttnProblem {
   const void* q;  // bf16, element (b, s, h, e) at b*sb + s*ss + h*sh + e

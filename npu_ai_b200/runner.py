@@ -346,14 +346,19 @@ class NpuGemm:
         return t
 
     def attention(self, q, k, v, heads: int, scale: float | None = None, skip_reshape: bool = False,
-                  skip_output_reshape: bool = False, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+                  skip_output_reshape: bool = False, out_dtype: torch.dtype | None = None, *,
+                  group=None) -> torch.Tensor:
         """softmax(Q K^T * scale) V for all (batch, head) pairs in ONE launch (bf16 in, f32 accumulate).
 
         q/k/v: (b, t, heads*d), or (b, heads, t, d) when skip_reshape. Returns (b, tq, heads*d) (or
         (b, heads, tq, d) when skip_output_reshape), f32 unless `out_dtype` (npu/xdna1_gemm.py:499-533).
+        `group` (a torch.distributed process group, every rank holding the whole block on its GPU) splits the pairs
+        over the group's ranks in contiguous ranges and all-gathers the result (npu_ai_b200.sharding).
         """
         t_start = time.perf_counter()
         qd, kd, vd = (self._attn_operand(t) for t in (q, k, v))
+        # Q read in place: the caller's device tensor itself reached the kernel (no host copy, cast or compaction)
+        q_inplace = isinstance(q, torch.Tensor) and q.is_cuda and q.data_ptr() == qd.data_ptr() and q.dtype == qd.dtype
         if skip_reshape:
             b, h, tq, d = qd.shape
             tk = kd.shape[2]
@@ -366,18 +371,23 @@ class NpuGemm:
             raise ValueError(f"attention shape tq={tq} tk={tk} d={d} b*h={b * h} is outside the kernel's range")
         key = (b, tq, tk, h, d)
         ev = self._events()
-        y = kernels.attention(qd, kd, vd, h, scale=scale, head_major_in=skip_reshape,
-                              head_major_out=skip_output_reshape, out_dtype=out_dtype or self.out_dtype)
+        if group is not None:
+            from .sharding import attention_sharded
+            y = attention_sharded(qd, kd, vd, h, group=group, scale=scale, head_major_in=skip_reshape,
+                                  head_major_out=skip_output_reshape, out_dtype=out_dtype or self.out_dtype)
+        else:
+            y = kernels.attention(qd, kd, vd, h, scale=scale, head_major_in=skip_reshape,
+                                  head_major_out=skip_output_reshape, out_dtype=out_dtype or self.out_dtype)
         with self._lock:
             sh = self.stats["attn_by_shape"].setdefault(key, [0, 0.0, 0.0, 0.0, 0.0, 0, 0.0])
             self._close("attn", ev, key)
             wall = time.perf_counter() - t_start
             sh[0] += 1
             sh[2] += wall
-            sh[5] += 1
+            sh[5] += int(q_inplace)
             sh[6] += wall
             self.stats["attn_fused_calls"] += 1
-            self.stats["attn_fused_q_inplace"] += 1
+            self.stats["attn_fused_q_inplace"] += int(q_inplace)
             self.stats["attn_fused_flops"] += 4.0 * b * h * tq * tk * d
             self.stats["attn_fused_seconds"] += wall
         return y

@@ -6,7 +6,7 @@ _npu_linear_forward (:146-158); with no NPU runtime present it takes its CPU fal
 pin the oracle (oracle.linear_ref). The module imports only numpy and torch at top level, so it loads here even
 though the NPU stack (aie.iron, pyxrt) is absent.
 
-Run in a container where the reference tree is mounted:  python tests/golden/make_golden.py [reference_root]
+Run where the reference tree is available:  python tests/golden/make_golden.py <reference_root>
 """
 import importlib.util
 import os
@@ -14,16 +14,16 @@ import sys
 
 import torch
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-NODE = os.path.join(REF, "comfyui", "custom_nodes", "comfyui_xdna1_npu", "__init__.py")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "linear_fallback.pt")
-
 # (M, K, N): the reference test's unaligned case (scripts/05-gemm-test.py:18) and small SD1.5-like shapes.
 SHAPES = [(100, 100, 100), (77, 320, 320), (20, 768, 64), (33, 640, 136), (5, 1280, 64)]
 
 
 def main() -> None:
-    spec = importlib.util.spec_from_file_location("reference_xdna1_node", NODE)
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <reference_root>")
+    node_file = os.path.join(sys.argv[1], "comfyui", "custom_nodes", "comfyui_xdna1_npu", "__init__.py")
+    spec = importlib.util.spec_from_file_location("reference_xdna1_node", node_file)
     node = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(node)
     assert node._RUNTIME is None, "the fallback path needs no NPU runtime"

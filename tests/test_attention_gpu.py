@@ -60,6 +60,39 @@ def test_baseline_blocks(cuda_device, shape, variant):
     _check(_run(q, k, v, H, out_dtype=torch.bfloat16, variant=variant), ref)
 
 
+def test_unet_batch16_self_attention_block(cuda_device):
+    """The batch-16 UNet's top-level self-attention (16, 8, 4096, 4096, 40) on the automatic variant, the
+    two-query-tile kernel the UNet step runs, in both output types."""
+    B, H, Sq, Skv, D = 16, 8, 4096, 4096, 40
+    q, k, v, ref = _block(B, H, Sq, Skv, D, 16)
+    _check(_run(q, k, v, H), ref)
+    _check(_run(q, k, v, H, out_dtype=torch.bfloat16), ref)
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+@pytest.mark.parametrize("shape,head_major", [((2, 8, 1024, 1024, 80), False), ((3, 5, 300, 77, 40), False),
+                                              ((2, 8, 256, 256, 160), True)])
+def test_pair_sharded_attention_ranks(cuda_device, world, shape, head_major):
+    """Every rank's part of a (batch, head)-pair-sharded block (npu_ai_b200.sharding: contiguous pair ranges, at
+    most three strided in-place views per rank), emulated for all ranks in one process and assembled as the
+    all-gather does, against the oracle on the whole block."""
+    from npu_ai_b200 import kernels
+    from npu_ai_b200.sharding import attention_shard, pair_width
+    B, H, Sq, Skv, D = shape
+    q, k, v, ref = _block(B, H, Sq, Skv, D, 5)
+    if head_major:
+        q, k, v = (t.view(B, t.shape[1], H, D).transpose(1, 2).contiguous() for t in (q, k, v))
+        ref = ref.view(B, Sq, H, D).transpose(1, 2)
+    qd, kd, vd = (t.to(cuda_device) for t in (q, k, v))
+    parts = [attention_shard(qd, kd, vd, H, r, world, head_major_in=head_major, out_dtype=torch.float32)
+             for r in range(world)]
+    kernels.check_status(cuda_device)
+    assert all(p.shape[0] == pair_width(B * H, world) for p in parts)
+    hm = torch.cat(parts)[:B * H].view(B, H, Sq, D)
+    got = hm if head_major else hm.permute(0, 2, 1, 3).reshape(B, Sq, H * D)
+    _check(got, ref)
+
+
 @pytest.mark.parametrize("shape", ["1x4x256x256x40", "1x4x512x256x80", "2x8x1024x1024x80"])
 def test_reference_script_shapes(cuda_device, shape):
     """The reference's default shapes with its input distribution (q, k ~ 1.5 N(0,1))."""

@@ -48,6 +48,8 @@ def test_reference_arm_matches_the_gpu_arm_metric(reference_line):
     import bench
     assert reference_line["metric"] == bench.METRIC  # the same metric name as the GPU arm's line
     assert reference_line["unit"] == "TFLOP/s"
+    assert reference_line["config"] == json.loads(json.dumps(bench.hotpath_config(1)))  # the GPU arm's config
+    assert "whole 70-op step" in reference_line["cpu_baseline"]["sample"]
 
 
 def test_reference_arm_other_ranks_exit_without_work():

@@ -69,7 +69,7 @@ def test_offload_node_end_to_end(cuda_device, unet_pair):
     with torch.no_grad():
         ref = base.apply_model(x, t, ctx).float()
     node = cn.NODE_CLASS_MAPPINGS["XDNA1NpuLinearOffload"]()   # the reference's workflow class name still resolves
-    (patched,) = node.apply(base, True, 64, 320, "time_embed,label_emb,emb_layers", "auto", 256)
+    (patched,) = node.apply(base, True, 64, 320, "time_embed,label_emb,emb_layers", "auto")
     with torch.no_grad():
         y1 = patched.apply_model(x, t, ctx).float()   # first call: takeover, discovery pass, gate + accuracy check
         y2 = patched.apply_model(x, t, ctx).float()
@@ -81,15 +81,18 @@ def test_offload_node_end_to_end(cuda_device, unet_pair):
     assert len(rt.tblocks) == 16, len(rt.tblocks)               # residual adds in the output GEMMs' epilogues
     assert len(rt.lnorms) == 48, len(rt.lnorms)                 # norm1/norm2/norm3 of each block
     assert not rt.pending_res
-    assert rt.attn.counts["gpu"] > 0 and rt.attn.decision, "attention never reached the fused kernel"
-    assert all(e <= 0.1 for e in rt.attn.max_err.values())
+    assert rt.attn.fused_calls > 0 and any(r.variant is not None for r in rt.attn.shapes.values()), \
+        "attention never reached the fused kernel"
+    assert all(r.max_rel_err <= 0.1 for r in rt.attn.shapes.values() if r.max_rel_err is not None)
+    # with the default gate every attention of an accelerated UNet call is fused (16 blocks x self + cross)
+    assert all(r.model_reason is None for r in rt.attn.shapes.values())
     assert torch.isfinite(y2).all()
     assert rel_l2_err(y2, ref) < 3e-2, rel_l2_err(y2, ref)
     assert rel_l2_err(y1, y2) < 1e-6
     status = cn.NODE_CLASS_MAPPINGS["B200Status"]().status(None)["result"][0]
     assert "NpuGemm[B200]" in status and "layers on GPU kernels: 160" in status and "GEGLU blocks fused: 16" in status
     cn.NODE_CLASS_MAPPINGS["B200Release"]().release(patched)
-    assert not rt.installed
+    assert not rt.patched
     assert all(not isinstance(m.forward, types.MethodType) or m.forward.__func__ is not cn._gpu_linear_forward
                for m in model.modules() if isinstance(m, torch.nn.Linear))
     assert all(not isinstance(m.forward, types.MethodType) or m.forward.__func__ is not cn._gpu_geglu_forward
@@ -209,3 +212,44 @@ def test_unet_channels_last_on_conv_kernels(cuda_device):
         assert rel_l2_err(y, ref) < 3e-2, rel_l2_err(y, ref)
     finally:
         cn.B200Release().release(patched)
+
+
+def test_unet_benchmarked_configuration_against_cpu_oracle(cuda_device):
+    """The configuration bench.py times: the channels-last bf16 SD1.5 UNet at the 64x64
+    latent, batch 2 (one prompt x CFG), through the node with convolutions on, so every Linear, attention, 3x3 and
+    1x1 convolution, GroupNorm, ResBlock, LayerNorm, upsampling and skip concatenation runs on this library's
+    kernels. Checked against the same bf16-valued weights and inputs in f32 on the CPU (the oracle's torch ops).
+
+    Tolerance: relative L2 <= 6e-2, and no worse than 1.5x (+ 5e-3) the error torch's own bf16 execution of the
+    same model on the same GPU shows against that f32 reference (the bf16 floor of this network: every activation
+    rounded to bf16 through 16 transformer blocks and 25 ResBlocks)."""
+    from npu_ai_b200 import comfy_nodes as cn
+    from npu_ai_b200.sd15_unet import build_unet
+    cpu_model = build_unet(seed=2, device="cpu", dtype=torch.bfloat16).float()
+    model = build_unet(seed=2, device=cuda_device, dtype=torch.bfloat16).to(memory_format=torch.channels_last)
+    x, t, ctx = _inputs(64, device="cpu")
+    xb, cb = x.to(torch.bfloat16), ctx.to(torch.bfloat16)
+    with torch.no_grad():
+        ref = cpu_model(xb.float(), t, cb.float())
+    xg = xb.to(cuda_device).contiguous(memory_format=torch.channels_last)
+    base = FakeModelPatcher(model)
+    with torch.no_grad():
+        torch_bf16 = base.apply_model(xg, t.to(cuda_device), cb.to(cuda_device)).float().cpu()
+    (patched,) = cn.B200LinearOffload().apply(base, True, 64, 320, "time_embed,label_emb,emb_layers", "auto", 1,
+                                              True)
+    try:
+        rt = cn._get_runtime()
+        fused_calls = rt.attn.fused_calls
+        with torch.no_grad():
+            y = patched.apply_model(xg, t.to(cuda_device), cb.to(cuda_device)).float().cpu()
+        assert len(rt.weights) == 160 and len(rt.resblocks) == 22 and len(rt.upsamples) == 3
+        # every attention call of the accelerated pass on the fused kernel (the discovery pass uses the model's)
+        assert rt.attn.fused_calls - fused_calls == 32
+    finally:
+        cn.B200Release().release(patched)
+    floor = rel_l2_err(torch_bf16, ref)
+    err = rel_l2_err(y, ref)
+    print(f"UNet 64x64 batch 2 vs f32 CPU: rel-L2 {err:.3e} (torch bf16 on the GPU: {floor:.3e})")
+    assert torch.isfinite(y).all()
+    assert err <= 6e-2, err
+    assert err <= 1.5 * floor + 5e-3, (err, floor)

@@ -39,7 +39,7 @@ def test_offload_node_keeps_the_reference_inputs_and_defaults():
     assert both["min_features"][1]["default"] == 320
     assert both["skip_names"][1]["default"] == "time_embed,label_emb,emb_layers"
     assert both["attention"][1]["default"] == "auto"
-    assert both["attn_min_tokens"][1]["default"] == 256
+    assert both["attn_min_tokens"][1]["default"] == 1  # every SD1.5 attention shape on the kernel
     assert cn.B200LinearOffload.RETURN_TYPES == ("MODEL",)
 
 
@@ -49,25 +49,35 @@ def test_attention_variants_cover_the_sd15_head_dims():
         assert v and 0 in v and len(set(v)) == len(v)
 
 
-@pytest.mark.parametrize("mode,mask,gqa,fits,tq,expect", [
-    ("auto", None, False, True, 4096, None),
-    ("gpu", None, False, True, 256, None),
-    ("off", None, False, True, 4096, "model"),
-    ("auto", torch.zeros(1), False, True, 4096, "model"),
-    ("auto", None, True, True, 4096, "model"),
-    ("auto", None, False, False, 4096, "model"),
-    ("auto", None, False, True, 77, "model"),
+@pytest.mark.parametrize("mode,mask,gqa,fits,tq,min_tokens,expect", [
+    ("auto", False, False, True, 4096, 1, None),
+    ("gpu", False, False, True, 256, 1, None),
+    ("auto", False, False, True, 64, 1, None),        # the SD1.5 middle block stays on the fused kernel
+    ("off", False, False, True, 4096, 1, "attention mode = off"),
+    ("auto", True, False, True, 4096, 1, "masked attention"),
+    ("auto", False, True, True, 4096, 1, "grouped-query attention"),
+    ("auto", False, False, False, 4096, 1, "outside the fused kernel's range"),
+    ("auto", False, False, True, 77, 256, "fewer than 256 query tokens"),
 ])
-def test_attention_gate_static_routing(mode, mask, gqa, fits, tq, expect):
-    gate = cn.AttentionGate()
-    gate.mode = mode
+def test_attention_gate_static_routing(mode, mask, gqa, fits, tq, min_tokens, expect):
+    gate = cn.AttentionGate(mode=mode, min_tokens=min_tokens)
     key = (2, tq, tq, 8, 40)
-    assert gate.decide_static(key, mask, gqa, fits) == expect
-    if expect == "model":
-        assert key in gate.reason and gate.reason[key]
-        assert str(key) in gate.table()  # the reason shows in the Status node's table
+    assert gate.model_route_reason(key, mask, gqa, fits) == expect
+    if expect is not None:
+        assert gate.shapes[key].model_reason == expect
+        assert str(key) in gate.table() and expect in gate.table()  # the reason shows in the Status node's table
+        gate.model_route_reason(key, mask, gqa, fits)
+        assert gate.shapes[key].model_reason == expect      # logged and recorded once
     else:
-        assert key not in gate.reason
+        assert key not in gate.shapes
+
+
+def test_default_gate_keeps_every_sd15_attention_on_the_kernel():
+    gate = cn.AttentionGate()
+    assert gate.mode == "auto" and gate.min_tokens == 1
+    for key in ((2, 4096, 4096, 8, 40), (2, 4096, 77, 8, 40), (2, 1024, 1024, 8, 80), (2, 256, 256, 8, 160),
+                (2, 64, 64, 8, 160), (2, 64, 77, 8, 160)):
+        assert gate.model_route_reason(key, False, False, True) is None
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the behaviour on a host without a CUDA device")

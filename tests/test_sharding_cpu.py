@@ -129,3 +129,73 @@ def test_rank_failure_surfaces_as_error_on_the_other_rank(tmp_path, mode):
     assert time.time() - t0 < 120
     survivor = (tmp_path / "rank0.txt").read_text()
     assert survivor.startswith(("failed", "init failed")), survivor
+
+
+# ---- attention over (batch, head) pairs split across ranks -------------------------------------------------------
+def test_pair_segments_tile_every_range():
+    from npu_ai_b200.sharding import pair_range, pair_segments, pair_width
+    for B, H in ((2, 8), (3, 5), (1, 7), (16, 8)):
+        pairs = B * H
+        for W in (1, 2, 3, 4, 5, 8):
+            covered = []
+            for r in range(W):
+                lo, hi = pair_range(pairs, W, r)
+                assert hi - lo <= pair_width(pairs, W)
+                segs = pair_segments(lo, hi, H)
+                assert len(segs) <= 3
+                for b0, b1, h0, h1 in segs:
+                    assert 0 <= b0 < b1 <= B and 0 <= h0 < h1 <= H and (b1 - b0 == 1 or (h0, h1) == (0, H))
+                    covered += [b * H + h for b in range(b0, b1) for h in range(h0, h1)]
+            assert covered == list(range(pairs)), (B, H, W)
+
+
+def _cpu_compute(q, k, v, heads, out, head_major_in, scale, variant):
+    """CPU stand-in for the kernel launch (the oracle's attention), writing the head-major output view."""
+    from oracle import attention_ref
+    o = attention_ref(q, k, v, heads, scale=scale, head_major=head_major_in)
+    if not head_major_in:
+        o = o.view(q.shape[0], q.shape[1], heads, -1).transpose(1, 2)
+    out.copy_(o.to(out.dtype))
+
+
+def _block(B, H, Sq, Skv, D, head_major):
+    g = torch.Generator().manual_seed(11)
+    shp = (lambda S: (B, H, S, D)) if head_major else (lambda S: (B, S, H * D))
+    return (torch.randn(*shp(Sq), generator=g).bfloat16(), torch.randn(*shp(Skv), generator=g).bfloat16(),
+            torch.randn(*shp(Skv), generator=g).bfloat16())
+
+
+def _attn_worker(rank, world, port, dims, head_major, out_path):
+    import torch.distributed as dist
+    from npu_ai_b200.sharding import attention_sharded
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.set_num_threads(1)
+        q, k, v = _block(*dims, head_major)
+        out = attention_sharded(q, k, v, dims[1], head_major_in=head_major, head_major_out=head_major,
+                                out_dtype=torch.float32, compute=_cpu_compute)
+        torch.save(out, out_path.format(rank))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,dims,head_major", [
+    (2, (2, 4, 24, 16, 8), False),
+    (3, (2, 4, 24, 16, 8), False),     # 8 pairs over 3 ranks: ranges cut through a batch's heads, uneven chunks
+    (3, (3, 5, 16, 9, 16), True),      # head-major in and out, odd head count
+])
+def test_attention_pairs_sharded_over_ranks_match_the_oracle(tmp_path, world, dims, head_major):
+    """Every rank computes its contiguous (batch, head) pair range and the all-gather assembles the block: each
+    rank's result equals the oracle on the whole block (host logic with a CPU stand-in for the kernel launch)."""
+    from oracle import attention_ref
+    out_path = str(tmp_path / "out{}.pt")
+    mp.start_processes(_attn_worker, args=(world, _free_port(), dims, head_major, out_path), nprocs=world,
+                       join=True, start_method="spawn")
+    q, k, v = _block(*dims, head_major)
+    ref = attention_ref(q, k, v, dims[1], head_major=head_major)
+    for r in range(world):
+        got = torch.load(out_path.format(r))
+        assert got.shape == ref.shape
+        assert torch.allclose(got, ref, atol=1e-6, rtol=1e-5), (r, float((got - ref).abs().max()))
