@@ -13,6 +13,7 @@ import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libnpub200.so")
+TORCH_OPS_PATH = os.path.join(HERE, "libnpub200_torch.so")
 
 OK, EINVAL, ECUDA, EUNSUPPORTED, EDEVICE = 0, -1, -2, -3, -4
 DTYPE_BF16, DTYPE_F32 = 0, 1
@@ -89,6 +90,27 @@ def load() -> ctypes.CDLL:
                 fn.argtypes = args
             _lib = lib
     return _lib
+
+
+_ops = None
+
+
+def torch_ops():
+    """torch.ops.npub200: the GEMM and the fused attention as torch operators (libnpub200_torch.so, a thin
+    TORCH_LIBRARY layer over this same C ABI, running on torch's current CUDA stream), or None when that library
+    is not built. Loads libnpub200.so first, so both bindings share one instance of the kernel library."""
+    global _ops
+    if _ops is not None:
+        return _ops
+    load()
+    if not os.path.exists(TORCH_OPS_PATH):
+        return None
+    with _lock:
+        if _ops is None:
+            import torch
+            torch.ops.load_library(TORCH_OPS_PATH)
+            _ops = torch.ops.npub200
+    return _ops
 
 
 def exported_symbols() -> list[str]:

@@ -1,7 +1,9 @@
 """Tensor-level calls into libnpub200: torch CUDA tensors in, pointers/strides through the C ABI, torch out.
 
 torch provides device memory and the current stream; the arithmetic runs in the sm_100a kernels of the
-library. Nothing here computes on the CPU, and there is no fallback when a kernel refuses a request.
+library. The GEMM and the attention go through the library's torch operators (torch.ops.npub200.gemm /
+.attention, libnpub200_torch.so) when that layer is built, else straight through ctypes; both reach the same C ABI
+and kernels. Nothing here computes on the CPU, and there is no fallback when a kernel refuses a request.
 """
 from __future__ import annotations
 
@@ -120,6 +122,9 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out
                 residual.stride(1) != 1:
             raise ValueError("residual must be a bf16 [M, N] matrix with contiguous rows")
         handle = None  # the residual entry point takes the weight itself
+    ops = _lib.torch_ops()
+    if ops is not None:
+        return ops.gemm(x, w, bias, out, int(variant), None, int(handle or 0), residual)
     ws = _gemm_workspace(x, None if handle is not None else w, M, K, N, variant)
     args_tail = (ctypes.c_void_p(bias.data_ptr()) if bias is not None else None,
                  _DT[bias.dtype] if bias is not None else _lib.DTYPE_BF16,
@@ -395,6 +400,10 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, sca
         out = torch.empty(shape, dtype=out_dtype, device=q.device)
     if out.dtype not in _DT or out.stride(-1) != 1:
         raise ValueError("attention output must be bf16/f32 with a contiguous last dimension")
+    ops = _lib.torch_ops()
+    if ops is not None:
+        return ops.attention(q, k, v, out, B, H, Sq, Skv, D, 0, 0, 0, bool(head_major_in), bool(head_major_out),
+                             float(scale), int(variant), None)
     os_ = (out.stride(0), out.stride(2), out.stride(1)) if head_major_out else (out.stride(0), out.stride(1), D)
     with torch.cuda.device(q.device):
         _lib.call("npub200_attention",

@@ -44,3 +44,21 @@ def test_error_mapping():
     with pytest.raises(RuntimeError):
         _lib.check(_lib.ECUDA, "x")
     _lib.check(_lib.OK, "x")
+
+
+def test_torch_operators_register_over_the_c_abi():
+    """libnpub200_torch.so registers npub200::gemm and npub200::attention with the torch dispatcher (a CUDA kernel
+    only: CPU tensors are refused, there is no CPU path)."""
+    import pytest
+    import torch
+    ops = _lib.torch_ops()
+    assert ops is not None, "libnpub200_torch.so is not built"
+    g = str(ops.gemm.default._schema)
+    a = str(ops.attention.default._schema)
+    assert g.startswith("npub200::gemm(Tensor x, Tensor w, Tensor? bias=None, Tensor? out=None, int variant=0")
+    assert a.startswith("npub200::attention(Tensor q, Tensor k, Tensor v, Tensor? out, int B, int H, int Sq, int Skv, "
+                        "int d, int q_row_stride, int kv_row_stride, int o_row_stride, bool head_major_in, "
+                        "bool head_major_out, float scale, int variant")
+    x = torch.zeros(4, 8, dtype=torch.bfloat16)
+    with pytest.raises(NotImplementedError):
+        ops.gemm(x, torch.zeros(16, 8, dtype=torch.bfloat16))
