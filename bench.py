@@ -29,7 +29,7 @@ Reported in the same JSON line:
     batch 2 (one prompt, 4 Euler steps per image) and the host CPU's batch-2 UNet call;
   * cpu_baseline: the reference's CPU fallback (F.linear / SDPA in f32 on bf16-rounded inputs) on a bounded
     sample of the step, on the host cores;
-  * clocks: nvidia-smi samples over a soak of step replays directly before and through the timed region.
+  * clocks: SM clock, power and throttle reasons sampled through NVML every ~1 ms during the timed region.
 `--impl reference` times that CPU path alone on the whole 70-op step, with all host threads.
 
 Other modes (not the driver's line):
@@ -134,60 +134,95 @@ class Dist:
 # clocks
 # ----------------------------------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clock / power / throttle-reason samples every 200 ms; windows are marked on the host clock."""
+    """SM clock, power and throttle-reason samples of this rank's GPU, read (never set) through NVML every ~1 ms
+    on a background thread, so even a timed region of a few tens of milliseconds holds 20+ samples; falls back to
+    `nvidia-smi -lms 200` where NVML is unavailable. Windows are marked on the host clock."""
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
     FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, uuids: list[str]):
-        self.uuids = [u.lower() for u in uuids]
-        self.samples: list[list] = []
+    def __init__(self, uuid: str, period_s: float = 0.001):
+        self.uuid = uuid
+        self.period_s = period_s
+        self.samples: list[tuple] = []   # (host time, sm MHz, max sm MHz, power W, {reason names})
+        self.source = None
+        self._stop = threading.Event()
         self.proc = None
         self.thread = None
 
+    def _start_nvml(self) -> bool:
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByUUID(self.uuid)
+            max_sm = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001 - any NVML failure selects the nvidia-smi sampler
+            return False
+        bits = {"hw_slowdown": pynvml.nvmlClocksThrottleReasonHwSlowdown,
+                "hw_thermal_slowdown": pynvml.nvmlClocksThrottleReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": pynvml.nvmlClocksThrottleReasonSwThermalSlowdown,
+                "sw_power_cap": pynvml.nvmlClocksThrottleReasonSwPowerCap}
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    rs = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                except Exception:  # noqa: BLE001
+                    break
+                self.samples.append((time.perf_counter(), sm, max_sm, pw, {n for n, b in bits.items() if rs & b}))
+                time.sleep(self.period_s)
+        self.source = f"NVML every {self.period_s * 1e3:.0f} ms"
+        self.thread = threading.Thread(target=loop, daemon=True)
+        self.thread.start()
+        return True
+
     def start(self):
+        if self._start_nvml():
+            return
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
+        want = self.uuid.lower().replace("gpu-", "")
+        num = lambda v: float(v) if v.replace(".", "", 1).isdigit() else float("nan")  # noqa: E731
 
         def reader():
             for line in self.proc.stdout:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) == 8:
-                    self.samples.append(parts + [time.perf_counter()])
+                p = [x.strip() for x in line.split(",")]
+                if len(p) == 8 and p[0].lower().replace("gpu-", "") == want:
+                    self.samples.append((time.perf_counter(), num(p[1]), num(p[2]), num(p[3]),
+                                         {n for n, v in zip(self.NAMES, p[4:]) if v.lower() == "active"}))
+        self.source = "nvidia-smi -lms 200"
         self.thread = threading.Thread(target=reader, daemon=True)
         self.thread.start()
 
     def stop(self) -> None:
-        if self.proc is None:
-            return
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self._stop.set()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
         if self.thread is not None:
             self.thread.join(timeout=2)
 
     def summary(self, t_begin: float, t_end: float, window: str) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        want = {u.lower().replace("gpu-", "") for u in self.uuids if u}
-        timed = [s for s in self.samples if t_begin <= s[8] <= t_end + 0.2]
-        mine = [s for s in timed if s[0].lower().replace("gpu-", "") in want] or timed
-        num = lambda v: v.replace(".", "", 1).isdigit()  # noqa: E731
-        sm = [float(s[1]) for s in mine if num(s[1])]
-        mx = [float(s[2]) for s in mine if num(s[2])]
-        pw = [float(s[3]) for s in mine if num(s[3])]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in mine for i in range(4) if s[4 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(mine),
-                "samples_under_load": sum(1 for p in pw if p >= 300.0),
-                "power_w_median": statistics.median(pw) if pw else None, "window": window}
+        if self.source is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"], "samples": 0}
+        mine = [s for s in list(self.samples) if t_begin <= s[0] <= t_end]
+        sm = [s[1] for s in mine if s[1] == s[1]]
+        pw = [s[3] for s in mine if s[3] == s[3]]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(s[2] for s in mine) if mine else None,
+                "reasons": sorted(set().union(*[s[4] for s in mine])) if mine else [],
+                "samples": len(mine), "samples_under_load": sum(1 for p in pw if p >= 300.0),
+                "power_w_median": statistics.median(pw) if pw else None, "window": window, "source": self.source}
 
 
 def _gpu_uuid(dev: int) -> str:
@@ -530,7 +565,7 @@ def run_ours(args, dist) -> None:
     torch.cuda.synchronize()
     kernels.check_status(device)
 
-    sampler = ClockSampler([_gpu_uuid(dist.local_rank)]) if dist.rank == 0 else None
+    sampler = ClockSampler(_gpu_uuid(dist.local_rank)) if dist.rank == 0 else None
     if sampler is not None:
         sampler.start()
     # The step runs as a CUDA graph. A twin graph carries timing events at the attention-block and GEMM M-group
@@ -543,15 +578,17 @@ def run_ours(args, dist) -> None:
     graph_ev.replay()
     torch.cuda.synchronize()
     kernels.check_status(device)
-    # Soak: replays for about 4.5 s right before the timed region, so the clock record holds enough samples of the
-    # GPU under this load (every rank replays the same count: the graphs hold collectives).
-    one = _time_graph(graph, 3)
-    soak = int(dist.max(float(min(20000, max(10, round(args.soak_s * 1e3 / max(one, 1e-3))))), device))
+    # Optional soak (--soak-s, default none): step replays right before the timed region, e.g. to time the step in
+    # the GPU's power-capped steady state (every rank replays the same count: the graphs hold collectives).
+    soak = 0
+    if args.soak_s > 0:
+        one = _time_graph(graph, 3)
+        soak = int(dist.max(float(min(20000, max(10, round(args.soak_s * 1e3 / max(one, 1e-3))))), device))
     dist.barrier()
     torch.cuda.synchronize()
-    t_soak = time.perf_counter()
     for _ in range(soak):
         graph.replay()
+    t_begin = time.perf_counter()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
@@ -562,8 +599,8 @@ def run_ours(args, dist) -> None:
     torch.cuda.synchronize()
     t_end = time.perf_counter()
     dist.barrier()
-    clocks = sampler.summary(t_soak, t_end, f"{soak} step replays ({soak * one / 1e3:.1f} s) directly before the "
-                                           "timed region, then the timed region") if sampler is not None else None
+    clocks = sampler.summary(t_begin, t_end, "the timed region" + (f", after a soak of {soak} step replays"
+                                                                  if soak else "")) if sampler is not None else None
     kernels.check_status(device)
     ms_local = t0.elapsed_time(t1) / args.steps
     ms = dist.max(ms_local, device)
@@ -604,7 +641,7 @@ def run_ours(args, dist) -> None:
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4),
                 "peak_kind": f"{peaks['source']} burst bf16 (cuBLAS 8192^3, best of 10): the timed region is "
-                             f"{args.steps} steps of about {ms:.2f} ms",
+                             f"{args.steps} steps of about {ms:.2f} ms" + (" after a soak" if soak else ""),
                 "frac_of_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4),
                 "kernel": "gemm_bf16_tcgen05_kernel (66 sweep launches per step)",
                 "algorithmic_bytes_per_launch": int(gemm_bytes / len(wl.gemms)),
@@ -867,7 +904,7 @@ def run_unet(args, dist) -> None:
     """--workload unet: the UNet leg alone on one configuration, its own JSON line."""
     device = torch.device("cuda", dist.local_rank)
     torch.cuda.set_device(device)
-    sampler = ClockSampler([_gpu_uuid(dist.local_rank)]) if dist.rank == 0 else None
+    sampler = ClockSampler(_gpu_uuid(dist.local_rank)) if dist.rank == 0 else None
     if sampler is not None:
         sampler.start()
     ub = UNetBench(dist, device)
@@ -985,8 +1022,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-unet", action="store_true", help="skip the UNet leg of the default run")
     ap.add_argument("--unet-latents", default="64,128",
                     help="latent sizes of the default run's batch-16 UNet leg (comma-separated)")
-    ap.add_argument("--soak-s", type=float, default=4.5,
-                    help="seconds of step replays right before the timed region (for the clock record)")
+    ap.add_argument("--soak-s", type=float, default=0.0,
+                    help="seconds of step replays right before the timed region (default none)")
     ap.add_argument("--case", default=None, help="time one kernel: gemm:M,K,N, attn:B,H,Sq,Skv,D, geglu:M,K,n, "
                                                    "conv:n,h,w,cin,cout, gn:n,h,w,c, ln:rows,c, up:n,c,h,w or "
                                                    "cat:n,ca,cb,h,w")

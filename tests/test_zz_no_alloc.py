@@ -98,6 +98,6 @@ def test_noalloc_rejects_oversize_scratch(cuda_device):
     w = torch.zeros(N, K, dtype=torch.bfloat16, device=cuda_device)
     b = torch.zeros(N, dtype=torch.bfloat16, device=cuda_device)
     out = torch.empty(M, N, device=cuda_device)
-    assert _scratch_need(x, w) > 4 * 8 * 1024 * 1024  # far above NPUB200_NOALLOC_SCRATCH_BYTES (8 MiB)
+    assert _scratch_need(x, w) > 3 * 8 * 1024 * 1024  # far above NPUB200_NOALLOC_SCRATCH_BYTES (8 MiB)
     with pytest.raises(ValueError, match="scratch"):
         _noalloc(x, w, b, out)
