@@ -221,8 +221,8 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(s[2] for s in mine) if mine else None,
                 "reasons": sorted(set().union(*[s[4] for s in mine])) if mine else [],
-                "samples": len(mine), "samples_under_load": sum(1 for p in pw if p >= 300.0),
-                "power_w_median": statistics.median(pw) if pw else None, "window": window, "source": self.source}
+                "samples": len(mine), "power_w_median": statistics.median(pw) if pw else None,
+                "window": window, "source": self.source}
 
 
 def _gpu_uuid(dev: int) -> str:

@@ -37,7 +37,8 @@ def attn_variants(head_dim: int) -> tuple[int, ...]:
     dp = (head_dim + 15) // 16 * 16
     keys = (64, 96, 128) if dp <= 64 else ((64, 128) if dp <= 128 else (64,))
     qts = (1, 2) if dp <= 192 else (1,)
-    return (0,) + tuple(1000 * qt + bn for qt in qts for bn in keys)
+    four = (4064,) if dp <= 64 else ()  # four Q tiles per CTA: 64-key tiles, head dims up to 64
+    return (0,) + tuple(1000 * qt + bn for qt in qts for bn in keys) + four
 
 
 def _log(msg: str) -> None:

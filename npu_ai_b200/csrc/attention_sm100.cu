@@ -12,10 +12,10 @@
 //
 // Two kernels share one structure (softmax warps, a TMA producer warp, an MMA warp) and differ in how many
 // 128-row query tiles a CTA owns:
-//   attention_fwd_qt2_tcgen05_kernel  two Q tiles (256 query rows) per CTA, one CTA per SM, 320 threads. Both tiles
-//       share every K/V tile, and one MMA thread per SM feeds the tensor core, so MMA issue never contends with
-//       another CTA's. Per key tile j the MMA order is P_0(j-1) V, S_0(j), P_1(j-1) V, S_1(j): while softmax
-//       warpgroup 0 works on S_0(j), the tensor core finishes tile 1's work and the other way round.
+//   attention_fwd_mq_tcgen05_kernel  QT = 2 or 4 Q tiles (256 or 512 query rows) per CTA, one CTA per SM, 64 + 128 QT
+//       threads. All tiles share every K/V tile, and one MMA thread per SM feeds the tensor core, so MMA issue never
+//       contends with another CTA's. Per key tile j the MMA order is P_0(j-1) V, S_0(j), P_1(j-1) V, S_1(j), ...:
+//       while one softmax warpgroup works on its S, the tensor core finishes the other tiles' work.
 //   attention_fwd_tcgen05_kernel      one Q tile per CTA with S double-buffered (S_j, S_{j+1}), 192 threads, up to
 //       two CTAs per SM: for grids too small to fill the GPU with 256-row CTAs, and head dims above 192.
 // Roles:
@@ -45,11 +45,12 @@ constexpr int kAttnBM = 128;           // query rows per Q tile (one softmax war
 constexpr int kSoftmaxWarps = 4;       // per Q tile
 constexpr int kAtomBytesPerRow = 128;  // one 128-byte swizzle atom row: 64 bf16
 // Of every 8 (key, key+1) pairs of a softmax row, this many take their exponentials from the FMA-pipe polynomial
-// (exp2_poly3) instead of the MUFU. Head dims up to 64 (the least MMA work per exponential) gain from moving 2 of 8
-// to the FP32 pipe; larger head dims measured best with none.
-template <int DP>
+// (exp2_poly3_x2) instead of the MUFU. Measured: head dims up to 64 (the least MMA work per exponential) gain from
+// moving 2 of 8 to the FP32 pipe with one or two Q tiles per CTA; with four Q tiles per CTA the issue slots the
+// polynomial takes cost more than the MUFU time it saves; larger head dims run best with none.
+template <int DP, int QT>
 constexpr int exp_poly_pairs_per8() {
-  return DP <= 64 ? 2 : 0;
+  return (DP <= 64 && QT <= 2) ? 2 : 0;
 }
 
 struct MapPos {
@@ -198,29 +199,34 @@ __device__ __forceinline__ float softmax_step(uint32_t s_addr, int kv0, int Skv,
   const float m_new = move ? mx : m;
   const float alpha = fast_exp2(m - m_new);  // 1 when unchanged, 0 on the first tile
   const float neg_m = -m_new;
-  float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  // P row into TMEM over this lane's S (already in registers): bf16 pairs, 32 keys = 16 columns per store.
+  // x = s * c - m and the row sums two keys per instruction (f32x2 FMA / add); P row into TMEM over this lane's S
+  // (already in registers): bf16 pairs, 32 keys = 16 columns per store.
+  const uint64_t c2 = f2_pack(c, c);
+  const uint64_t nm2 = f2_pack(neg_m, neg_m);
+  uint64_t rs2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
   for (int c32 = 0; c32 < BN / 32; ++c32) {
     uint32_t pk[16];
 #pragma unroll
     for (int e2 = 0; e2 < 16; ++e2) {
-      const float x0 = fmaf(s[c32 * 32 + 2 * e2], c, neg_m);
-      const float x1 = fmaf(s[c32 * 32 + 2 * e2 + 1], c, neg_m);
-      const bool poly = (e2 & 7) >= 8 - POLY;
-      const float p0 = poly ? exp2_poly3(x0) : fast_exp2(x0);
-      const float p1 = poly ? exp2_poly3(x1) : fast_exp2(x1);
-      rs8[(2 * e2) & 7] += p0;
-      rs8[(2 * e2 + 1) & 7] += p1;
+      float x0, x1, p0, p1;
+      f2_unpack(f2_fma(f2_pack(s[c32 * 32 + 2 * e2], s[c32 * 32 + 2 * e2 + 1]), c2, nm2), x0, x1);
+      if ((e2 & 7) >= 8 - POLY) {
+        exp2_poly3_x2(x0, x1, p0, p1);
+      } else {
+        p0 = fast_exp2(x0);
+        p1 = fast_exp2(x1);
+      }
+      rs2[e2 & 3] = f2_add(rs2[e2 & 3], f2_pack(p0, p1));
       pk[e2] = pack_bf16x2(p0, p1);
     }
     tmem_st16(s_addr + uint32_t(c32 * 16), pk);
   }
-#pragma unroll
-  for (int w = 4; w >= 1; w >>= 1)
-#pragma unroll
-    for (int e = 0; e < w; ++e) rs8[e] += rs8[e + w];
-  l = l * alpha + rs8[0];
+  rs2[0] = f2_add(rs2[0], rs2[2]);
+  rs2[1] = f2_add(rs2[1], rs2[3]);
+  float r0, r1;
+  f2_unpack(f2_add(rs2[0], rs2[1]), r0, r1);
+  l = l * alpha + (r0 + r1);
   m = m_new;
   return alpha;
 }
@@ -481,8 +487,8 @@ __global__ void __launch_bounds__(kAttn1Threads, Attn1Layout<DP, BN, STAGES>::kT
       tc_fence_after();
       // P_j overwrites S_j; P_{j-2} V_{j-2}, the last reader of these columns, completed before s_full of tile j.
       bool move;
-      const float alpha = softmax_step<BN, exp_poly_pairs_per8<DP>()>(lane_base + uint32_t(L::kSCol + buf * BN), j * BN, args.Skv, c,
-                                           args.rescale_thr, m, l, move);
+      const float alpha = softmax_step<BN, exp_poly_pairs_per8<DP, 1>()>(
+          lane_base + uint32_t(L::kSCol + buf * BN), j * BN, args.Skv, c, args.rescale_thr, m, l, move);
       // O correction (rare with the lazy max): O_row *= alpha once P_{j-1} V_{j-1} has landed.
       if (j > 0 && __any_sync(0xffffffffu, move)) {
         if (!mbar_wait_bounded(&pv_done[(j - 1) & 1], uint32_t((j - 1) >> 1) & 1u, abort_flag, args.ctl,
@@ -518,52 +524,61 @@ __global__ void __launch_bounds__(kAttn1Threads, Attn1Layout<DP, BN, STAGES>::kT
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Kernel 2: two Q tiles (256 query rows) per CTA sharing every K/V tile. Warps 0-3 softmax of Q tile 0, warps 4-7
-// of Q tile 1 (warp w reaches TMEM lanes 32*(w%4)..+31), warp 8 producer, warp 9 MMA.
-// SB S buffers per Q tile (2 when 2 * (2 BN + DP) TMEM columns fit, else 1):
-//   SB = 2  MMA step t issues P_w(t-2) V then S_w(t) into the buffer P_w(t-2) occupied, for w = 0, 1. S_w(t) goes
-//           out as soon as the softmax has finished tile t-2, a whole softmax step before it is needed.
+// Kernel 2: QT Q tiles (QT x 128 query rows, QT = 2 or 4) per CTA sharing every K/V tile. Softmax warps 4w..4w+3
+// serve Q tile w (warp v reaches TMEM lanes 32*(v%4)..+31, so each scheduler holds one warp of every Q tile), warp
+// 4 QT is the producer, warp 4 QT + 1 the MMA issuer. More Q tiles per SM mean more softmax warps in flight per
+// scheduler: the softmax of d <= 64 heads is latency-bound, not throughput-bound.
+// SB S buffers per Q tile (2 when QT * (2 BN + DP) TMEM columns fit, else 1):
+//   SB = 2  MMA step t issues P_w(t-2) V then S_w(t) into the buffer P_w(t-2) occupied, for every Q tile w.
+//           S_w(t) goes out as soon as the softmax has finished tile t-2, a whole softmax step before it is needed.
 //   SB = 1  MMA step t issues P_w(t-1) V then S_w(t): the softmax of a Q tile waits for its own P V and next S,
-//           and the other Q tile's softmax fills that gap.
+//           and the other Q tiles' softmax warps fill that gap.
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int kAttn2Threads = 320;
+template <int QT>
+constexpr int attn_mq_threads() {
+  return QT * kSoftmaxWarps * 32 + 64;
+}
 
-template <int DP, int BN, int STAGES>
-struct Attn2Layout {
+template <int DP, int BN, int STAGES, int QT>
+struct AttnMqLayout {
   static constexpr int kNA = (DP + 63) / 64;
   static constexpr int kQAtom = kAttnBM * kAtomBytesPerRow;  // 16 KB
   static constexpr int kKVAtom = BN * kAtomBytesPerRow;
   static constexpr int kQBytes = kNA * kQAtom;    // one Q tile
   static constexpr int kKVBytes = kNA * kKVAtom;  // one K (or V) tile
-  static constexpr int kQOff = 0;                 // Q tile 0, then Q tile 1
-  static constexpr int kKOff = kQOff + 2 * kQBytes;
+  static constexpr int kQOff = 0;                 // Q tiles 0..QT-1
+  static constexpr int kKOff = kQOff + QT * kQBytes;
   static constexpr int kVOff = kKOff + STAGES * kKVBytes;
   static constexpr int kBarOff = kVOff + STAGES * kKVBytes;
-  static constexpr int SB = (2 * (2 * BN + DP) <= 512) ? 2 : 1;  // S buffers per Q tile
-  // q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2][SB], p_full[2][SB], pv_done[2], o_full[2],
+  static constexpr int SB = (QT * (2 * BN + DP) <= 512) ? 2 : 1;  // S buffers per Q tile
+  // q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[QT][SB], p_full[QT][SB], pv_done[QT], o_full[QT],
   // drain. p_full has one barrier per S buffer: with SB = 2 a softmax warpgroup may finish tiles j and j+1 before
   // the MMA warp consumes tile j, and a single barrier would then complete two phases under one wait.
-  static constexpr int kNumBars = 1 + 4 * STAGES + 4 * SB + 4 + 1;
+  static constexpr int kNumBars = 1 + 4 * STAGES + 2 * QT * SB + 2 * QT + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
-  // TMEM: S_0[0..SB) | S_1[0..SB) | O_0 | O_1. P_w(j) overwrites the first BN/2 columns of the S buffer it came from.
-  static constexpr int kSCol = 0;            // S_w[b] at (w * SB + b) * BN
-  static constexpr int kOCol = 2 * SB * BN;  // O_w at kOCol + w * DP
-  static constexpr int kTmemUsed = kOCol + 2 * DP;
+  // TMEM: S_0[0..SB) | ... | S_{QT-1}[0..SB) | O_0 | ... | O_{QT-1}. P_w(j) overwrites the first BN/2 columns of the
+  // S buffer it came from.
+  static constexpr int kSCol = 0;             // S_w[b] at (w * SB + b) * BN
+  static constexpr int kOCol = QT * SB * BN;  // O_w at kOCol + w * DP
+  static constexpr int kTmemUsed = kOCol + QT * DP;
   static constexpr int kTmemCols = (kTmemUsed <= 128) ? 128 : (kTmemUsed <= 256) ? 256 : 512;
+  static_assert(QT == 2 || QT == 4, "two or four Q tiles per CTA");
   static_assert(DP % 16 == 0 && DP >= 16 && DP <= 192, "padded head dim must be a multiple of 16 in [16, 192]");
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 128, "key tile must be 64, 96 or 128");
-  static_assert(kTmemUsed <= 512, "S buffers + two O tiles must fit in 512 TMEM columns");
+  static_assert(kTmemUsed <= 512, "S buffers + the O tiles must fit in 512 TMEM columns");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
-template <int DP, int BN, int STAGES>
-__global__ void __launch_bounds__(kAttn2Threads, 1)
-    attention_fwd_qt2_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_q,
-                                     const __grid_constant__ CUtensorMap tm_k,
-                                     const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
-  using L = Attn2Layout<DP, BN, STAGES>;
+template <int DP, int BN, int STAGES, int QT>
+__global__ void __launch_bounds__(attn_mq_threads<QT>(), 1)
+    attention_fwd_mq_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                    const __grid_constant__ CUtensorMap tm_k,
+                                    const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
+  using L = AttnMqLayout<DP, BN, STAGES, QT>;
   constexpr int SB = L::SB;
+  constexpr int kProducerWarp = QT * kSoftmaxWarps;
+  constexpr int kMmaWarp = kProducerWarp + 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::kQOff;
@@ -576,16 +591,16 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   uint64_t* k_empty = v_full + STAGES;
   uint64_t* v_empty = k_empty + STAGES;
   uint64_t* s_full = v_empty + STAGES;  // [w * SB + b]
-  uint64_t* p_full = s_full + 2 * SB;   // [w * SB + b]
-  uint64_t* pv_done = p_full + 2 * SB;
-  uint64_t* o_full = pv_done + 2;
-  uint64_t* drain = o_full + 2;
+  uint64_t* p_full = s_full + QT * SB;  // [w * SB + b]
+  uint64_t* pv_done = p_full + QT * SB;
+  uint64_t* o_full = pv_done + QT;
+  uint64_t* drain = o_full + QT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * (2 * kAttnBM);
+  const int q0 = blockIdx.x * (QT * kAttnBM);
   const int pair = blockIdx.y;
   const int hh = pair % args.H;
   const int bb = pair / args.H;
@@ -599,11 +614,11 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 2 * SB; ++i) {
+    for (int i = 0; i < QT * SB; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], kSoftmaxWarps);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < QT; ++i) {
       mbar_init(&pv_done[i], 1);
       mbar_init(&o_full[i], 1);
     }
@@ -611,7 +626,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, L::kTmemCols);
     tmem_relinquish();
     tc_fence_before();
@@ -621,7 +636,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   const uint32_t tmem_base = *tmem_slot;
   pdl_launch_dependents();
 
-  if (warp == 8) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -629,8 +644,8 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       tma_prefetch_desc(&tm_v);
       pdl_wait();  // q/k/v may be the previous kernel's outputs
       int c0, c1, c2, c3;
-      mbar_arrive_expect_tx(q_full, 2 * L::kQBytes);
-      for (int w = 0; w < 2; ++w)
+      mbar_arrive_expect_tx(q_full, QT * L::kQBytes);
+      for (int w = 0; w < QT; ++w)
         for (int a = 0; a < L::kNA; ++a) {
           map_coords(args.pq, a, q0 + w * kAttnBM, hh, bb, c0, c1, c2, c3);
           tma_load_4d(&tm_q, q_full, sQ + w * L::kQBytes + a * L::kQAtom, c0, c1, c2, c3);
@@ -639,7 +654,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
                                       bb);
       mbar_wait_drain(q_full, 0, args.ctl);
     }
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     // The whole warp runs the loop (operands stay warp-uniform); one elected lane issues the MMAs and their commits.
     bool ok = true;
@@ -654,7 +669,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     // Step t, for each Q tile w: O_w += P_w(t-SB) V_{t-SB}, then S_w(t) = Q_w K_t^T into the S buffer P_w(t-SB)
     // occupied (issued after the P V that reads it). The last SB steps only finish the P V products.
     for (int t = 0; ok && t < nkv + SB; ++t) {
-      for (int w = 0; w < 2; ++w) {
+      for (int w = 0; w < QT; ++w) {
         if (t >= SB) {
           const int i = t - SB;
           const int st = i % STAGES;
@@ -674,7 +689,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
                              tmem_base + uint32_t(L::kSCol + (w * SB + i % SB) * BN),
                              v_desc + uint64_t((st * L::kKVBytes) >> 4), i > 0);
             if (SB == 2) umma_commit(&pv_done[w]);
-            if (w == 1) umma_commit(&v_empty[st]);
+            if (w == QT - 1) umma_commit(&v_empty[st]);
             if (i == nkv - 1) umma_commit(&o_full[w]);
           }
           __syncwarp();
@@ -694,7 +709,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
                             q_desc + uint64_t((w * L::kQBytes) >> 4), k_desc + uint64_t((st * L::kKVBytes) >> 4),
                             L::kQAtom, L::kKVAtom);
             umma_commit(&s_full[w * SB + t % SB]);
-            if (w == 1) umma_commit(&k_empty[st]);
+            if (w == QT - 1) umma_commit(&k_empty[st]);
           }
           __syncwarp();
         }
@@ -706,7 +721,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       mbar_wait_drain(drain, 0u, args.ctl);
     }
   } else {
-    // ------------------------------------------------------------------ softmax / correction / epilogue (warps 0-7)
+    // ------------------------------------------------------------------ softmax / correction / epilogue
     const int w = warp >> 2;  // Q tile
     const int wq = warp & 3;  // TMEM lane quarter
     const uint32_t lane_base = tmem_base + (uint32_t(wq * 32) << 16);
@@ -724,8 +739,9 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       }
       tc_fence_after();
       bool move;
-      const float alpha = softmax_step<BN, exp_poly_pairs_per8<DP>()>(lane_base + uint32_t(L::kSCol + (w * SB + b) * BN), j * BN, args.Skv, c,
-                                           args.rescale_thr, m, l, move);
+      const uint32_t s_addr = lane_base + uint32_t(L::kSCol + (w * SB + b) * BN);
+      const float alpha =
+          softmax_step<BN, exp_poly_pairs_per8<DP, QT>()>(s_addr, j * BN, args.Skv, c, args.rescale_thr, m, l, move);
       // O correction (rare with the lazy max), once P_w(j-1) V_{j-1} has landed. With one S buffer it has: it was
       // issued before S_w(j), whose commit fired s_full.
       if (j > 0 && __any_sync(0xffffffffu, move)) {
@@ -753,7 +769,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   }
 
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
   }
@@ -840,12 +856,13 @@ int launch_qt1(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& 
                        kAttn1Threads, &configured[device], mq, mk, mv, a, grid, st);
 }
 
-template <int DP, int BN, int STAGES>
-int launch_qt2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnArgs& a, dim3 grid,
-               cudaStream_t st, int device) {
+template <int DP, int BN, int STAGES, int QT>
+int launch_mq(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnArgs& a, dim3 grid,
+              cudaStream_t st, int device) {
   static bool configured[64] = {false};
-  return launch_kernel(attention_fwd_qt2_tcgen05_kernel<DP, BN, STAGES>, Attn2Layout<DP, BN, STAGES>::kSmemBytes,
-                       kAttn2Threads, &configured[device], mq, mk, mv, a, grid, st);
+  return launch_kernel(attention_fwd_mq_tcgen05_kernel<DP, BN, STAGES, QT>,
+                       AttnMqLayout<DP, BN, STAGES, QT>::kSmemBytes, attn_mq_threads<QT>(), &configured[device], mq,
+                       mk, mv, a, grid, st);
 }
 
 // Kernel variant for a padded head dim, key tile and Q tiles per CTA.
@@ -854,7 +871,9 @@ int launch_for(int64_t DP, int BN, int QT, const CUtensorMap& mq, const CUtensor
 #define NPUB200_ATTN_QT1(dp, bn, stages) \
   if (QT == 1 && DP == dp && BN == bn) return launch_qt1<dp, bn, stages>(mq, mk, mv, a, grid, st, dev);
 #define NPUB200_ATTN_QT2(dp, bn, stages) \
-  if (QT == 2 && DP == dp && BN == bn) return launch_qt2<dp, bn, stages>(mq, mk, mv, a, grid, st, dev);
+  if (QT == 2 && DP == dp && BN == bn) return launch_mq<dp, bn, stages, 2>(mq, mk, mv, a, grid, st, dev);
+#define NPUB200_ATTN_QT4(dp, bn, stages) \
+  if (QT == 4 && DP == dp && BN == bn) return launch_mq<dp, bn, stages, 4>(mq, mk, mv, a, grid, st, dev);
   // One Q tile per CTA. d <= 64 with 64-key tiles: two CTAs per SM.
   NPUB200_ATTN_QT1(16, 64, 5)
   NPUB200_ATTN_QT1(32, 64, 5)
@@ -909,8 +928,14 @@ int launch_for(int64_t DP, int BN, int QT, const CUtensorMap& mq, const CUtensor
   NPUB200_ATTN_QT2(160, 64, 2)
   NPUB200_ATTN_QT2(176, 64, 2)
   NPUB200_ATTN_QT2(192, 64, 2)
+  // Four Q tiles per CTA (one CTA per SM, 16 softmax warps), 64-key tiles, one S buffer per Q tile: d <= 64.
+  NPUB200_ATTN_QT4(16, 64, 6)
+  NPUB200_ATTN_QT4(32, 64, 6)
+  NPUB200_ATTN_QT4(48, 64, 6)
+  NPUB200_ATTN_QT4(64, 64, 6)
 #undef NPUB200_ATTN_QT1
 #undef NPUB200_ATTN_QT2
+#undef NPUB200_ATTN_QT4
   return fail(kErrUnsupported, "no attention variant for padded head dim %lld with %d-key tiles and %d Q tiles per CTA",
               (long long)DP, BN, QT);
 }
@@ -929,22 +954,25 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   for (const void* ptr : {p.q, p.k, p.v})
     if (reinterpret_cast<uintptr_t>(ptr) & 15u) return fail(kErrInvalid, "q/k/v base addresses must be 16-byte aligned");
   const int64_t DP = (p.D + 15) / 16 * 16;
-  // variant = key tile (0 = automatic, 64, 128) + 1000 * Q tiles per CTA (0 = automatic, 1, 2).
+  // variant = key tile (0 = automatic, 64, 96, 128) + 1000 * Q tiles per CTA (0 = automatic, 1, 2, 4).
   const int QT_req = p.variant / 1000;
   int BN = p.variant % 1000;
-  if (p.variant < 0 || QT_req > 2 || (BN != 0 && BN != 64 && BN != 96 && BN != 128))
-    return fail(kErrUnsupported, "attention variant %d (key tile 0/64/96/128 plus 1000 x Q tiles per CTA 0/1/2)",
+  if (p.variant < 0 || QT_req == 3 || QT_req > 4 || (BN != 0 && BN != 64 && BN != 96 && BN != 128))
+    return fail(kErrUnsupported, "attention variant %d (key tile 0/64/96/128 plus 1000 x Q tiles per CTA 0/1/2/4)",
                 p.variant);
+  if (QT_req == 4 && (DP > 64 || (BN != 0 && BN != 64)))
+    return fail(kErrUnsupported, "four Q tiles per CTA need head dim <= 64 and 64-key tiles (variant %d)", p.variant);
   // Automatic choice (measured on the SD1.5 blocks at batch 2 and 16):
-  //   d <= 64       96-key tiles; two Q tiles per CTA once the grid of one-tile CTAs (two per SM) is at least 8 waves
-  //                 deep, one Q tile otherwise (shorter pipeline fill per CTA).
+  //   d <= 64       four Q tiles per CTA with 64-key tiles once there are at least 3 x SMs one-tile CTAs' worth of
+  //                 query tiles ((2, 8, 4096, 4096, 40): 99 us against 102 us with two Q tiles and 112 us with one;
+  //                 batch 16: 662 against 679 and 729 us); one Q tile with 96-key tiles for smaller grids.
   //   64 < d <= 128 one Q tile; 64-key tiles (two CTAs per SM) when the grid fills two per SM, else 128.
   //   d > 128       64-key tiles; two Q tiles per CTA when one-tile CTAs would take more than one wave.
   const int64_t ctas_qt1 = (p.Sq + kAttnBM - 1) / kAttnBM * pairs;
   const int64_t sms = dev->sms;
   int QT = QT_req;
   if (DP <= 64) {
-    if (QT == 0) QT = ctas_qt1 >= 8 * 2 * sms ? 2 : 1;
+    if (QT == 0) QT = ctas_qt1 >= 3 * sms ? 4 : 1;
     if (BN == 0) BN = 96;
   } else if (DP <= 128) {
     if (QT == 0) QT = 1;
@@ -955,6 +983,7 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   }
   if (QT == 2 && DP > 192) return fail(kErrUnsupported, "two Q tiles per CTA need head dim <= 192");
   if (BN == 96 && DP > 64) BN = 64;
+  if (QT == 4) BN = 64;
 
   const int q_rows = QT * kAttnBM;
   CUtensorMap mq, mk, mv;

@@ -446,21 +446,46 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
-// 2^x on the FMA pipe, so a share of a softmax's exponentials leaves the MUFU (16 per clock per SM) for the
-// FP32 pipe: x = n + f with n = round(x) (adding 1.5 * 2^23 leaves round(x) in the low mantissa bits) and
+// Two f32 lanes in one 64-bit register and the sm_100 packed f32x2 arithmetic on them (one FMA-pipe instruction
+// for two results).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x of two values on the FMA pipe (packed f32x2 arithmetic), so a share of a softmax's exponentials leaves the
+// MUFU (16 per clock per SM) for the FP32 pipe: x = n + f with n = round(x) (adding 1.5 * 2^23 leaves round(x) in the low mantissa bits) and
 // f in [-1/2, 1/2]; 2^f = 1 + f (c1 + f (c2 + f c3)) with coefficients from a minimax fit of the relative error by
 // linear programming (fit_exp2_poly.py beside this file; max relative error 1.01e-4, a fortieth of a bf16 ulp); 2^n
 // is added into the exponent field. x is clamped at -125 so the result stays a normal float: masked keys
 // (x = -inf) give 2^-125 instead of 0, which no bf16 P or f32 row sum can see.
-__device__ __forceinline__ float exp2_poly3(float x) {
-  x = fmaxf(x, -125.0f);
-  const float t = x + 12582912.0f;
-  const float n = t - 12582912.0f;
-  const float f = x - n;
-  float p = fmaf(5.500893667e-02f, f, 2.422109544e-01f);
-  p = fmaf(p, f, 6.932829022e-01f);
-  p = fmaf(p, f, 1.0f);
-  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+__device__ __forceinline__ void exp2_poly3_x2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t x = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t t = f2_add(x, f2_pack(12582912.0f, 12582912.0f));
+  const uint64_t n = f2_add(t, f2_pack(-12582912.0f, -12582912.0f));
+  const uint64_t f = f2_fma(n, f2_pack(-1.0f, -1.0f), x);
+  uint64_t p = f2_fma(f2_pack(5.500893667e-02f, 5.500893667e-02f), f, f2_pack(2.422109544e-01f, 2.422109544e-01f));
+  p = f2_fma(p, f, f2_pack(6.932829022e-01f, 6.932829022e-01f));
+  p = f2_fma(p, f, f2_pack(1.0f, 1.0f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {

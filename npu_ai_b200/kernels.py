@@ -368,8 +368,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, sca
 
     q/k/v: bf16 CUDA tensors, (B, S, H*D) or (B, H, S, D) when head_major_in; the output (B, Sq, H*D) or
     (B, H, Sq, D) when head_major_out. Strides may be padded (views), the last dimension must be contiguous.
-    variant: key tile (0 = automatic, 64, 128) + 1000 x query tiles of 128 rows per CTA (0 = automatic, 1, 2);
-    e.g. 2128 = two query tiles with 128-key tiles.
+    variant: key tile (0 = automatic, 64, 96, 128) + 1000 x query tiles of 128 rows per CTA (0 = automatic, 1, 2,
+    or 4 with 64-key tiles for head dims up to 64); e.g. 2128 = two query tiles with 128-key tiles.
     """
     for name, t in (("q", q), ("k", k), ("v", v)):
         _require_cuda(t, name)

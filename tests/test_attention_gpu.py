@@ -60,6 +60,17 @@ def test_baseline_blocks(cuda_device, shape, variant):
     _check(_run(q, k, v, H, out_dtype=torch.bfloat16, variant=variant), ref)
 
 
+@pytest.mark.parametrize("shape", [(2, 8, 4096, 4096, 40), (2, 8, 4096, 77, 40), (1, 1, 1, 1, 40), (1, 2, 100, 300, 40),
+                                   (1, 2, 1000, 129, 64), (3, 5, 600, 257, 16), (1, 3, 513, 1000, 32)])
+def test_four_query_tiles_per_cta(cuda_device, shape):
+    """The four-Q-tile kernel (variant 4064: 512 query rows per CTA, 64-key tiles, d <= 64), full and ragged
+    shapes whose trailing Q tiles lie partly or wholly past Sq."""
+    B, H, Sq, Skv, D = shape
+    q, k, v, ref = _block(B, H, Sq, Skv, D, 3)
+    _check(_run(q, k, v, H, variant=4064), ref)
+    _check(_run(q, k, v, H, out_dtype=torch.bfloat16, variant=4064), ref)
+
+
 def test_unet_batch16_self_attention_block(cuda_device):
     """The batch-16 UNet's top-level self-attention (16, 8, 4096, 4096, 40) on the automatic variant, the
     two-query-tile kernel the UNet step runs, in both output types."""
