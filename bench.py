@@ -660,6 +660,7 @@ def run_ours(args, dist) -> None:
                           "last step (graph replay); average launch duration = segment time / launches"}
 
     e2e = None if args.no_e2e else run_e2e(args, dist, device, total)
+    roofline["attention_sharded"] = sharded_attention_leg(dist, device)
     kernels.check_status(device)
     del graph, graph_ev  # graphs holding NCCL calls go before the process group
     wl.release()
@@ -680,6 +681,49 @@ def run_ours(args, dist) -> None:
                 "execution": "CUDA graph of the step (PDL between kernels), replayed per step",
                 "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "unet": unet}
         print(json.dumps(line), flush=True)
+
+
+def sharded_attention_leg(dist, device, reps: int = 10) -> dict:
+    """One fixed attention block (the 64x64-latent self-attention, (2, 8, 4096, 4096, 40)) split over the ranks
+    by (batch, head) pairs (npu_ai_b200.sharding): every rank holds the whole block, runs the fused kernel on its
+    contiguous pair range, and one NCCL all-gather assembles the (B, Sq, H*d) result on every rank. Strong
+    scaling of one block; the all-gather and the head-major -> (B, Sq, H*d) relayout are reported apart from the
+    kernel time, against the unsharded launch on one GPU. Device times (CUDA events), median over `reps` calls,
+    max over ranks."""
+    from npu_ai_b200 import kernels
+    from npu_ai_b200.sharding import attention_sharded, pair_width, resolve_timings
+    B, H, Sq, Skv, D = ATTN_BLOCKS[0]
+    q, k, v = (_seeded((B, S, H * D), 1.0, 900 + i, device) for i, S in ((0, Sq), (1, Skv), (2, Skv)))
+    out = torch.empty((B, Sq, H * D), dtype=torch.bfloat16, device=device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    one = []
+    for i in range(reps + 3):
+        e0.record()
+        kernels.attention(q, k, v, H, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            one.append(e0.elapsed_time(e1))
+    res = {"block": [B, H, Sq, Skv, D], "ranks": dist.world, "unsharded_us": round(statistics.median(one) * 1e3, 1)}
+    if dist.world == 1:
+        return res
+    parts = []
+    for i in range(reps + 3):
+        tm = {}
+        attention_sharded(q, k, v, H, timings=tm, out_dtype=torch.bfloat16)
+        r = resolve_timings(tm)
+        if i >= 3:
+            parts.append(r)
+    kern = dist.max(statistics.median(p["kernel_ms"] for p in parts), device)
+    gath = dist.max(statistics.median(p["gather_ms"] for p in parts), device)
+    rel = dist.max(statistics.median(p["relayout_ms"] for p in parts), device)
+    total = kern + gath + rel
+    res.update({"pairs_per_rank": pair_width(B * H, dist.world), "kernel_us": round(kern * 1e3, 1),
+                "gather_us": round(gath * 1e3, 1), "relayout_us": round(rel * 1e3, 1),
+                "total_us": round(total * 1e3, 1), "speedup_vs_unsharded": round(statistics.median(one) / total, 3),
+                "gather_bytes_per_rank": parts[0]["gather_bytes_per_rank"],
+                "note": "the scatter is free (inputs resident on every rank); the gather moves (N-1)/N of the output"})
+    return res
 
 
 def run_e2e(args, dist, device, total_flops) -> dict:

@@ -253,3 +253,34 @@ def test_unet_benchmarked_configuration_against_cpu_oracle(cuda_device):
     assert torch.isfinite(y).all()
     assert err <= 6e-2, err
     assert err <= 1.5 * floor + 5e-3, (err, floor)
+
+
+def test_runner_pool_leased_operands_like_reference_attention_script(cuda_device):
+    """The reference's attention test (scripts/11-attn-fused-test.py:101-112, --pinned) leases buffers from the
+    runner's pool, copies q/k/v into row-padded views of them and passes the views to attention(): the same here,
+    with the views read in place by the fused kernel (the lease is reused after release)."""
+    from npu_ai_b200.runner import NpuGemm
+    from oracle import attention_ref, rel_max_err
+    gemm = NpuGemm(device=cuda_device, verbose=False)
+    b, h, tq, tk, d = 1, 4, 256, 256, 40
+    pad = (h * d + 127) // 128 * 128
+    g = torch.Generator().manual_seed(0)
+    src = [torch.randn(b, t, h * d, generator=g) * s for t, s in ((tq, 1.5), (tk, 1.5), (tk, 1.0))]
+    views, bufs = [], []
+    for i, t in enumerate(src):
+        buf = gemm.pool.lease(("TEST", i, b, t.shape[1], pad), b * t.shape[1], pad, torch.bfloat16)
+        view = buf.t2d.view(b, t.shape[1], pad)[:, :, :h * d]
+        view.copy_(t)
+        views.append(view)
+        bufs.append(buf)
+    assert gemm.stats["buffers"] == 3 and gemm.stats["buffer_bytes"] > 0
+    o = gemm.attention(*views, h)
+    torch.cuda.synchronize()
+    assert gemm.stats["attn_fused_q_inplace"] == 1   # the padded pool view reached the kernel without a copy
+    q, k, v = (t.to(torch.bfloat16) for t in src)
+    assert rel_max_err(o, attention_ref(q, k, v, h)) < 0.1
+    assert float((o.float().cpu() - attention_ref(q, k, v, h)).abs().max()) <= 2e-2
+    for buf in bufs:
+        buf.release()
+    again = gemm.pool.lease(("TEST", 0, b, tq, pad), b * tq, pad, torch.bfloat16)
+    assert again is bufs[0] and gemm.stats["buffers"] == 3   # released buffers are reused, not reallocated
