@@ -649,12 +649,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
         for (int c0 = half * cw; c0 < kOutCols; c0 += 2 * cw) {
           const bool chunk_tma = args.tma_store && c0 + cw <= kOutCols;
-          if (chunk_tma) {
-            if (lane == 0) bulk_wait_read<0>();  // this warp's previous store has read the staging tile
-            __syncwarp();
+          // This warp's previous TMA store must have read the staging tile before the first staging write of this
+          // chunk; waiting only there lets that read overlap this chunk's TMEM loads and arithmetic.
+          bool staged = false;
+          auto stage_wait = [&]() {
+            if (!staged) {
+              if (lane == 0) bulk_wait_read<0>();
+              __syncwarp();
+              staged = true;
+            }
+          };
+          // The chunk's 32-column groups: both TMEM loads of a 64-column chunk are issued before one wait.
+          uint32_t racc[2][32];
+          if constexpr (!GEGLU) {
+            tmem_ld32(t_row + uint32_t(c0), racc[0]);
+            if (c0 + 32 < min(c0 + cw, kOutCols)) tmem_ld32(t_row + uint32_t(c0 + 32), racc[1]);
+            tmem_wait_ld();
           }
-#pragma unroll 1
-          for (int c = c0; c < min(c0 + cw, kOutCols); c += 32) {
+#pragma unroll
+          for (int sub = 0; sub < 2; ++sub) {
+            const int c = c0 + 32 * sub;
+            if (c >= min(c0 + cw, kOutCols)) break;
             // Bias of the 32 columns from column offset `off` of the tile (the table) or of the output (own row).
             auto fetch_bias = [&](float (&bb)[32], int off, int gcol) {
               if (table_bias) {
@@ -696,13 +711,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
               }
             } else {
-              {
-                uint32_t r[32];
-                tmem_ld32(t_row + uint32_t(c), r);
-                tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-              }
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(racc[sub][j]);
               float b[32];
               fetch_bias(b, c, n0 + c);
 #pragma unroll
@@ -710,6 +720,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               if (args.residual != nullptr) add_residual32(args, m0 + row, n0 + c, v);
             }
             if (chunk_tma) {
+              stage_wait();
               uint8_t* rowp = sb + lane * 128;
               if (args.out_f32) {
 #pragma unroll
