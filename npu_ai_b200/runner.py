@@ -251,7 +251,7 @@ class NpuGemm:
             return None
         b = _as_tensor(bias)
         if b.device != self.device:
-            b = b.to(self.device)
+            b = b.to(self.device, non_blocking=b.is_pinned())  # stream-ordered: no host sync for pinned biases
         if b.dtype not in (torch.float32, torch.bfloat16):
             b = b.float()
         return b.contiguous()
