@@ -963,16 +963,28 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   if (QT_req == 4 && (DP > 64 || (BN != 0 && BN != 64)))
     return fail(kErrUnsupported, "four Q tiles per CTA need head dim <= 64 and 64-key tiles (variant %d)", p.variant);
   // Automatic choice (measured on the SD1.5 blocks at batch 2 and 16):
-  //   d <= 64       four Q tiles per CTA with 64-key tiles once there are at least 3 x SMs one-tile CTAs' worth of
-  //                 query tiles ((2, 8, 4096, 4096, 40): 99 us against 102 us with two Q tiles and 112 us with one;
-  //                 batch 16: 662 against 679 and 729 us); one Q tile with 96-key tiles for smaller grids.
+  //   d <= 64       with at least 3 x SMs one-tile CTAs' worth of query tiles: four Q tiles per CTA with 64-key
+  //                 tiles, or two with 96-key tiles when that wastes less of the last wave. The model: time ~ waves x
+  //                 Q tiles per CTA x cost per tile, the four-tile kernel's cost per tile 0.98 of the two-tile one's
+  //                 (measured: (2, 8, 4096, 4096, 40) 97 us with four, 1 wave, against 101 us with two, 2 waves;
+  //                 batch 16 648 against 661 us, 7 against 14 waves). (2, 8, 16384, 16384, 40) is 3.46 waves of
+  //                 four-tile CTAs against 6.92 of two-tile ones, so it takes two. One Q tile with 96-key tiles for
+  //                 smaller grids.
   //   64 < d <= 128 one Q tile; 64-key tiles (two CTAs per SM) when the grid fills two per SM, else 128.
   //   d > 128       64-key tiles; two Q tiles per CTA when one-tile CTAs would take more than one wave.
   const int64_t ctas_qt1 = (p.Sq + kAttnBM - 1) / kAttnBM * pairs;
   const int64_t sms = dev->sms;
   int QT = QT_req;
   if (DP <= 64) {
-    if (QT == 0) QT = ctas_qt1 >= 3 * sms ? 4 : 1;
+    if (QT == 0) {
+      QT = 1;
+      if (ctas_qt1 >= 3 * sms) {
+        const int64_t tiles = (p.Sq + kAttnBM - 1) / kAttnBM;  // 128-row query tiles per (b, h) pair
+        const int64_t waves4 = ((tiles + 3) / 4 * pairs + sms - 1) / sms;
+        const int64_t waves2 = ((tiles + 1) / 2 * pairs + sms - 1) / sms;
+        QT = (double(waves4) * 4.0 * 0.98 <= double(waves2) * 2.0) ? 4 : 2;
+      }
+    }
     if (BN == 0) BN = 96;
   } else if (DP <= 128) {
     if (QT == 0) QT = 1;
