@@ -10,12 +10,12 @@
 // (K/V interleaving, Q slabs, parts), its tiling limits (tq % 4bq, tk % bk, bh % 4; xdna1_program.py:422-426) and
 // the per-head fallback: any Sq/Skv works here, the key tail (e.g. Skv = 77) is masked in the kernel.
 //
-// Two kernels share one structure (softmax warps, a TMA producer warp, an MMA warp) and differ in how many
+// Two kernels share one structure (softmax warps, a TMA producer warp, MMA-issuing warps) and differ in how many
 // 128-row query tiles a CTA owns:
-//   attention_fwd_mq_tcgen05_kernel  QT = 2 or 4 Q tiles (256 or 512 query rows) per CTA, one CTA per SM, 64 + 128 QT
-//       threads. All tiles share every K/V tile, and one MMA thread per SM feeds the tensor core, so MMA issue never
-//       contends with another CTA's. Per key tile j the MMA order is P_0(j-1) V, S_0(j), P_1(j-1) V, S_1(j), ...:
-//       while one softmax warpgroup works on its S, the tensor core finishes the other tiles' work.
+//   attention_fwd_mq_tcgen05_kernel  QT = 2 or 4 Q tiles (256 or 512 query rows) per CTA, one CTA per SM, 96 + 128 QT
+//       threads. All tiles share every K/V tile. One warp issues every S = Q K^T into a ring of S buffers shared by
+//       the tiles (ahead of need, as buffers free up), another every O += P V, so a tile's next S no longer waits
+//       behind its own P V and the other tiles' MMAs.
 //   attention_fwd_tcgen05_kernel      one Q tile per CTA with S double-buffered (S_j, S_{j+1}), 192 threads, up to
 //       two CTAs per SM: for grids too small to fill the GPU with 256-row CTAs, and head dims above 192.
 // Roles:
@@ -25,10 +25,10 @@
 //                  when m moves, and normalises + stores O at the end.
 //   producer warp  TMA: Q once, then K and V tiles into STAGES-deep rings, K one tile ahead of V. A K slot is
 //                  released as soon as its S MMAs complete, a V slot when its P V MMAs complete.
-//   MMA warp       TMEM owner + tcgen05 issuer: S = Q K_j^T (M=128, N=BN, both K-major in shared memory) and
+//   MMA warp(s)    TMEM owner + tcgen05 issue: S = Q K_j^T (M=128, N=BN, both K-major in shared memory) and
 //                  O += P V_j (P from TMEM, V MN-major in shared memory). tcgen05.mma ops of one thread execute in
-//                  issue order, so S_{j+1} (or S_{j+2}) may overwrite the columns holding P_j once P_j V_j has been
-//                  issued, and a tcgen05.commit covers every MMA issued before it.
+//                  issue order and a tcgen05.commit covers every MMA its thread issued before it; between the two
+//                  issuers of kernel 2 the order comes from mbarriers (a buffer is refilled only after its P V).
 // Data layout: every operand lives in shared memory as 128-byte-swizzled atoms of 64 head-dim (or key) columns,
 // loaded by TMA with 128-byte rows from a 4-D (dim, head, seq, batch) tensor map over the caller's strided
 // tensor. The map's innermost extent is the true head dim, so the columns past it (40 -> 64, 80 -> 128,
@@ -525,18 +525,25 @@ __global__ void __launch_bounds__(kAttn1Threads, Attn1Layout<DP, BN, STAGES>::kT
 
 // ---------------------------------------------------------------------------------------------------------------
 // Kernel 2: QT Q tiles (QT x 128 query rows, QT = 2 or 4) per CTA sharing every K/V tile. Softmax warps 4w..4w+3
-// serve Q tile w (warp v reaches TMEM lanes 32*(v%4)..+31, so each scheduler holds one warp of every Q tile), warp
-// 4 QT is the producer, warp 4 QT + 1 the MMA issuer. More Q tiles per SM mean more softmax warps in flight per
-// scheduler: the softmax of d <= 64 heads is latency-bound, not throughput-bound.
-// SB S buffers per Q tile (2 when QT * (2 BN + DP) TMEM columns fit, else 1):
-//   SB = 2  MMA step t issues P_w(t-2) V then S_w(t) into the buffer P_w(t-2) occupied, for every Q tile w.
-//           S_w(t) goes out as soon as the softmax has finished tile t-2, a whole softmax step before it is needed.
-//   SB = 1  MMA step t issues P_w(t-1) V then S_w(t): the softmax of a Q tile waits for its own P V and next S,
-//           and the other Q tiles' softmax warps fill that gap.
+// serve Q tile w (warp v reaches TMEM lanes 32*(v%4)..+31, so each scheduler holds one warp of every Q tile); warp
+// 4 QT is the TMA producer, warp 4 QT + 1 issues every S = Q K^T and warp 4 QT + 2 every O += P V. More Q tiles
+// per SM mean more softmax warps in flight per scheduler: the softmax of d <= 64 heads is latency-bound.
+// With one MMA warp serving the tiles in order (P_w(t-1) V then S_w(t), tile after tile), each tile's next S waited
+// for that warp's whole round: per tile two barrier waits, 7 tcgen05.mma at d <= 64 (S: K = 48 in 3; P V: 64 keys
+// in 4) and their commits took ~600 cycles of latency (clock64 timeline on B200), and a d = 40 softmax warpgroup
+// idled most of each key step. So S is issued ahead of need by its own warp, and P V by another:
+//   * TMEM holds NB S buffers shared by the Q tiles as a ring, then the QT O accumulators. S number k = t QT + w
+//     (key tile t, Q tile w) goes into buffer k % NB as soon as the P V of S number k - NB has completed: with
+//     NB > QT the next S of a tile is computed while its softmax still works on the current one.
+//   * P_w(t) is written as bf16 pairs over the first BN/2 columns of the buffer S_w(t) came from. The P V issuer
+//     takes the P's in the same order and frees each buffer with a commit after its P V (buf_free).
+//   * The softmax rescales O_w only after P_w(t-1) V has completed (pv_done[w]). NB <= 2 QT keeps that wait's
+//     parity unambiguous: S_w(t) went out after the P V of S number tQT + w - NB, so the issuer's in-order
+//     completion had already finished P_w(t-2) V.
 // ---------------------------------------------------------------------------------------------------------------
 template <int QT>
 constexpr int attn_mq_threads() {
-  return QT * kSoftmaxWarps * 32 + 64;
+  return QT * kSoftmaxWarps * 32 + 3 * 32;  // softmax warpgroups, TMA producer, S issuer, P V issuer
 }
 
 template <int DP, int BN, int STAGES, int QT>
@@ -550,23 +557,19 @@ struct AttnMqLayout {
   static constexpr int kKOff = kQOff + QT * kQBytes;
   static constexpr int kVOff = kKOff + STAGES * kKVBytes;
   static constexpr int kBarOff = kVOff + STAGES * kKVBytes;
-  static constexpr int SB = (QT * (2 * BN + DP) <= 512) ? 2 : 1;  // S buffers per Q tile
-  // q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[QT][SB], p_full[QT][SB], pv_done[QT], o_full[QT],
-  // drain. p_full has one barrier per S buffer: with SB = 2 a softmax warpgroup may finish tiles j and j+1 before
-  // the MMA warp consumes tile j, and a single barrier would then complete two phases under one wait.
-  static constexpr int kNumBars = 1 + 4 * STAGES + 2 * QT * SB + 2 * QT + 1;
+  // TMEM (all 512 columns): S buffers 0..NB-1 at b * BN, then O_w at kOCol + w * DP.
+  static constexpr int kTmemCols = 512;
+  static constexpr int kOCol = kTmemCols - QT * DP;
+  static constexpr int NB = (kOCol / BN < 2 * QT) ? kOCol / BN : 2 * QT;
+  // q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[NB], p_full[NB], buf_free[NB], pv_done[QT],
+  // o_full[QT], drain[2] (one per issuing warp).
+  static constexpr int kNumBars = 1 + 4 * STAGES + 3 * NB + 2 * QT + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
-  // TMEM: S_0[0..SB) | ... | S_{QT-1}[0..SB) | O_0 | ... | O_{QT-1}. P_w(j) overwrites the first BN/2 columns of the
-  // S buffer it came from.
-  static constexpr int kSCol = 0;             // S_w[b] at (w * SB + b) * BN
-  static constexpr int kOCol = QT * SB * BN;  // O_w at kOCol + w * DP
-  static constexpr int kTmemUsed = kOCol + QT * DP;
-  static constexpr int kTmemCols = (kTmemUsed <= 128) ? 128 : (kTmemUsed <= 256) ? 256 : 512;
   static_assert(QT == 2 || QT == 4, "two or four Q tiles per CTA");
   static_assert(DP % 16 == 0 && DP >= 16 && DP <= 192, "padded head dim must be a multiple of 16 in [16, 192]");
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 128, "key tile must be 64, 96 or 128");
-  static_assert(kTmemUsed <= 512, "S buffers + the O tiles must fit in 512 TMEM columns");
+  static_assert(NB >= QT, "every Q tile needs an S buffer next to the O tiles in 512 TMEM columns");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -576,9 +579,10 @@ __global__ void __launch_bounds__(attn_mq_threads<QT>(), 1)
                                     const __grid_constant__ CUtensorMap tm_k,
                                     const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
   using L = AttnMqLayout<DP, BN, STAGES, QT>;
-  constexpr int SB = L::SB;
+  constexpr int NB = L::NB;
   constexpr int kProducerWarp = QT * kSoftmaxWarps;
-  constexpr int kMmaWarp = kProducerWarp + 1;
+  constexpr int kSWarp = kProducerWarp + 1;   // S issuer; owns the TMEM allocation
+  constexpr int kPvWarp = kProducerWarp + 2;  // P V issuer
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::kQOff;
@@ -590,11 +594,12 @@ __global__ void __launch_bounds__(attn_mq_threads<QT>(), 1)
   uint64_t* v_full = k_full + STAGES;
   uint64_t* k_empty = v_full + STAGES;
   uint64_t* v_empty = k_empty + STAGES;
-  uint64_t* s_full = v_empty + STAGES;  // [w * SB + b]
-  uint64_t* p_full = s_full + QT * SB;  // [w * SB + b]
-  uint64_t* pv_done = p_full + QT * SB;
-  uint64_t* o_full = pv_done + QT;
-  uint64_t* drain = o_full + QT;
+  uint64_t* s_full = v_empty + STAGES;  // [buffer]
+  uint64_t* p_full = s_full + NB;       // [buffer]
+  uint64_t* buf_free = p_full + NB;     // [buffer]
+  uint64_t* pv_done = buf_free + NB;    // [Q tile]
+  uint64_t* o_full = pv_done + QT;      // [Q tile]
+  uint64_t* drain = o_full + QT;        // [issuer]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
 
@@ -605,6 +610,7 @@ __global__ void __launch_bounds__(attn_mq_threads<QT>(), 1)
   const int hh = pair % args.H;
   const int bb = pair / args.H;
   const int nkv = args.nkv;
+  const int total = nkv * QT;  // S (and P V) products of the CTA, numbered k = t QT + w
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -614,19 +620,21 @@ __global__ void __launch_bounds__(attn_mq_threads<QT>(), 1)
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < QT * SB; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], kSoftmaxWarps);
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], kSoftmaxWarps);
+      mbar_init(&buf_free[b], 1);
     }
     for (int i = 0; i < QT; ++i) {
       mbar_init(&pv_done[i], 1);
       mbar_init(&o_full[i], 1);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == kSWarp) {
     tmem_alloc(tmem_slot, L::kTmemCols);
     tmem_relinquish();
     tc_fence_before();
@@ -654,71 +662,74 @@ __global__ void __launch_bounds__(attn_mq_threads<QT>(), 1)
                                       bb);
       mbar_wait_drain(q_full, 0, args.ctl);
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------ MMA issuer
-    // The whole warp runs the loop (operands stay warp-uniform); one elected lane issues the MMAs and their commits.
+  } else if (warp == kSWarp || warp == kPvWarp) {
+    // ------------------------------------------------------------------ MMA issuers
+    // The whole warp runs the loop (operands stay warp-uniform); one elected lane issues the MMAs and commits.
+    const bool s_role = warp == kSWarp;
+    uint64_t* my_drain = &drain[s_role ? 0 : 1];
     bool ok = true;
     if (args.ctl.debug & 1u) {
-      if (!mbar_wait_bounded_warp(drain, 0, abort_flag, args.ctl, kStatusForced)) ok = false;
+      if (!mbar_wait_bounded_warp(my_drain, 0, abort_flag, args.ctl, kStatusForced)) ok = false;
     }
-    if (ok && !mbar_wait_bounded_warp(q_full, 0, abort_flag, args.ctl, kStatusTimeoutMma)) ok = false;
-    tc_fence_after();
-    const uint64_t q_desc = smem_desc_kmajor_sw128(smem_u32(sQ));
-    const uint64_t k_desc = smem_desc_kmajor_sw128(smem_u32(sK));
-    const uint64_t v_desc = smem_desc_mnmajor_sw128(smem_u32(sV), L::kKVAtom);
-    // Step t, for each Q tile w: O_w += P_w(t-SB) V_{t-SB}, then S_w(t) = Q_w K_t^T into the S buffer P_w(t-SB)
-    // occupied (issued after the P V that reads it). The last SB steps only finish the P V products.
-    for (int t = 0; ok && t < nkv + SB; ++t) {
-      for (int w = 0; w < QT; ++w) {
-        if (t >= SB) {
-          const int i = t - SB;
-          const int st = i % STAGES;
-          if (w == 0 && !mbar_wait_bounded_warp(&v_full[st], uint32_t(i / STAGES) & 1u, abort_flag, args.ctl,
-                                                kStatusTimeoutMma)) {
-            ok = false;
-            break;
-          }
-          if (!mbar_wait_bounded_warp(&p_full[w * SB + i % SB], uint32_t(i / SB) & 1u, abort_flag, args.ctl,
-                                      kStatusTimeoutMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          if (elect_one()) {
-            issue_pv<DP, BN>(tmem_base + uint32_t(L::kOCol + w * DP),
-                             tmem_base + uint32_t(L::kSCol + (w * SB + i % SB) * BN),
-                             v_desc + uint64_t((st * L::kKVBytes) >> 4), i > 0);
-            if (SB == 2) umma_commit(&pv_done[w]);
-            if (w == QT - 1) umma_commit(&v_empty[st]);
-            if (i == nkv - 1) umma_commit(&o_full[w]);
-          }
-          __syncwarp();
+    if (s_role) {
+      // S_w(t) = Q_w K_t^T into buffer k % NB, once the P V that last read that buffer has completed.
+      if (ok && !mbar_wait_bounded_warp(q_full, 0, abort_flag, args.ctl, kStatusTimeoutMma)) ok = false;
+      tc_fence_after();
+      const uint64_t q_desc = smem_desc_kmajor_sw128(smem_u32(sQ));
+      const uint64_t k_desc = smem_desc_kmajor_sw128(smem_u32(sK));
+      for (int k = 0; ok && k < total; ++k) {
+        const int t = k / QT, w = k % QT, b = k % NB, n = k / NB;
+        const int st = t % STAGES;
+        if (n > 0 && !mbar_wait_bounded_warp(&buf_free[b], uint32_t(n - 1) & 1u, abort_flag, args.ctl,
+                                             kStatusTimeoutMma)) {
+          ok = false;
+          break;
         }
-        if (t < nkv) {
-          const int st = t % STAGES;
-          if (w == 0) {
-            if (!mbar_wait_bounded_warp(&k_full[st], uint32_t(t / STAGES) & 1u, abort_flag, args.ctl,
-                                        kStatusTimeoutMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-          }
-          if (elect_one()) {
-            issue_s<DP, BN>(tmem_base + uint32_t(L::kSCol + (w * SB + t % SB) * BN),
-                            q_desc + uint64_t((w * L::kQBytes) >> 4), k_desc + uint64_t((st * L::kKVBytes) >> 4),
-                            L::kQAtom, L::kKVAtom);
-            umma_commit(&s_full[w * SB + t % SB]);
-            if (w == QT - 1) umma_commit(&k_empty[st]);
-          }
-          __syncwarp();
+        if (w == 0 && !mbar_wait_bounded_warp(&k_full[st], uint32_t(t / STAGES) & 1u, abort_flag, args.ctl,
+                                              kStatusTimeoutMma)) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        if (elect_one()) {
+          issue_s<DP, BN>(tmem_base + uint32_t(b * BN), q_desc + uint64_t((w * L::kQBytes) >> 4),
+                          k_desc + uint64_t((st * L::kKVBytes) >> 4), L::kQAtom, L::kKVAtom);
+          umma_commit(&s_full[b]);
+          if (w == QT - 1) umma_commit(&k_empty[st]);
+        }
+        __syncwarp();
+      }
+    } else {
+      // O_w += P_w(t) V_t from buffer k % NB, in the order the S products went out; each commit frees the buffer.
+      const uint64_t v_desc = smem_desc_mnmajor_sw128(smem_u32(sV), L::kKVAtom);
+      for (int k = 0; ok && k < total; ++k) {
+        const int t = k / QT, w = k % QT, b = k % NB, n = k / NB;
+        const int st = t % STAGES;
+        if (w == 0 && !mbar_wait_bounded_warp(&v_full[st], uint32_t(t / STAGES) & 1u, abort_flag, args.ctl,
+                                              kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait_bounded_warp(&p_full[b], uint32_t(n) & 1u, abort_flag, args.ctl, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (elect_one()) {
+          issue_pv<DP, BN>(tmem_base + uint32_t(L::kOCol + w * DP), tmem_base + uint32_t(b * BN),
+                           v_desc + uint64_t((st * L::kKVBytes) >> 4), t > 0);
+          umma_commit(&buf_free[b]);
+          umma_commit(&pv_done[w]);
+          if (w == QT - 1) umma_commit(&v_empty[st]);
+          if (t == nkv - 1) umma_commit(&o_full[w]);
+        }
+        __syncwarp();
       }
     }
     if (!ok) {
-      if (elect_one()) umma_commit(drain);
+      if (elect_one()) umma_commit(my_drain);
       __syncwarp();
-      mbar_wait_drain(drain, 0u, args.ctl);
+      mbar_wait_drain(my_drain, 0u, args.ctl);
     }
   } else {
     // ------------------------------------------------------------------ softmax / correction / epilogue
@@ -731,22 +742,19 @@ __global__ void __launch_bounds__(attn_mq_threads<QT>(), 1)
     float l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      const int b = j % SB;
-      if (!mbar_wait_bounded(&s_full[w * SB + b], uint32_t(j / SB) & 1u, abort_flag, args.ctl,
-                             kStatusTimeoutEpilogue)) {
+      const int k = j * QT + w;
+      const int b = k % NB;
+      if (!mbar_wait_bounded(&s_full[b], uint32_t(k / NB) & 1u, abort_flag, args.ctl, kStatusTimeoutEpilogue)) {
         ok = false;
         break;
       }
       tc_fence_after();
       bool move;
-      const uint32_t s_addr = lane_base + uint32_t(L::kSCol + (w * SB + b) * BN);
-      const float alpha =
-          softmax_step<BN, exp_poly_pairs_per8<DP, QT>()>(s_addr, j * BN, args.Skv, c, args.rescale_thr, m, l, move);
-      // O correction (rare with the lazy max), once P_w(j-1) V_{j-1} has landed. With one S buffer it has: it was
-      // issued before S_w(j), whose commit fired s_full.
+      const float alpha = softmax_step<BN, exp_poly_pairs_per8<DP, QT>()>(lane_base + uint32_t(b * BN), j * BN,
+                                                                           args.Skv, c, args.rescale_thr, m, l, move);
+      // O correction (rare with the lazy max), once P_w(j-1) V_{j-1} has completed.
       if (j > 0 && __any_sync(0xffffffffu, move)) {
-        if (SB == 2 && !mbar_wait_bounded(&pv_done[w], uint32_t(j - 1) & 1u, abort_flag, args.ctl,
-                                          kStatusTimeoutEpilogue)) {
+        if (!mbar_wait_bounded(&pv_done[w], uint32_t(j - 1) & 1u, abort_flag, args.ctl, kStatusTimeoutEpilogue)) {
           ok = false;
           break;
         }
@@ -756,7 +764,7 @@ __global__ void __launch_bounds__(attn_mq_threads<QT>(), 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[w * SB + b]);
+      if (lane == 0) mbar_arrive(&p_full[b]);
     }
     if (ok && nkv >= 1) {
       pdl_wait();  // the previous kernel may still read the output buffer
@@ -769,7 +777,7 @@ __global__ void __launch_bounds__(attn_mq_threads<QT>(), 1)
   }
 
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kSWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
   }
@@ -963,29 +971,18 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   if (QT_req == 4 && (DP > 64 || (BN != 0 && BN != 64)))
     return fail(kErrUnsupported, "four Q tiles per CTA need head dim <= 64 and 64-key tiles (variant %d)", p.variant);
   // Automatic choice (measured on the SD1.5 blocks at batch 2 and 16):
-  //   d <= 64       with at least 3 x SMs one-tile CTAs' worth of query tiles: four Q tiles per CTA with 64-key
-  //                 tiles, or two with 96-key tiles when that wastes less of the last wave. The model: time ~ waves x
-  //                 Q tiles per CTA x cost per tile, the four-tile kernel's cost per tile 0.98 of the two-tile one's
-  //                 (measured: (2, 8, 4096, 4096, 40) 97 us with four, 1 wave, against 101 us with two, 2 waves;
-  //                 batch 16 648 against 661 us, 7 against 14 waves). (2, 8, 16384, 16384, 40) is 3.46 waves of
-  //                 four-tile CTAs against 6.92 of two-tile ones, so it takes two. One Q tile with 96-key tiles for
-  //                 smaller grids.
+  //   d <= 64       with at least 3 x SMs one-tile CTAs' worth of query tiles: two Q tiles per CTA with 128-key
+  //                 tiles (three S buffers in the ring): (2, 8, 4096, 4096, 40) 88 us against 94 with 96-key tiles
+  //                 and 96 with four Q tiles; batch 16 592 against 639 / 642 us; (2, 8, 16384, 16384, 40) 1106
+  //                 against 1186 / 1401 us. One Q tile with 96-key tiles for smaller grids.
   //   64 < d <= 128 one Q tile; 64-key tiles (two CTAs per SM) when the grid fills two per SM, else 128.
   //   d > 128       64-key tiles; two Q tiles per CTA when one-tile CTAs would take more than one wave.
   const int64_t ctas_qt1 = (p.Sq + kAttnBM - 1) / kAttnBM * pairs;
   const int64_t sms = dev->sms;
   int QT = QT_req;
   if (DP <= 64) {
-    if (QT == 0) {
-      QT = 1;
-      if (ctas_qt1 >= 3 * sms) {
-        const int64_t tiles = (p.Sq + kAttnBM - 1) / kAttnBM;  // 128-row query tiles per (b, h) pair
-        const int64_t waves4 = ((tiles + 3) / 4 * pairs + sms - 1) / sms;
-        const int64_t waves2 = ((tiles + 1) / 2 * pairs + sms - 1) / sms;
-        QT = (double(waves4) * 4.0 * 0.98 <= double(waves2) * 2.0) ? 4 : 2;
-      }
-    }
-    if (BN == 0) BN = 96;
+    if (QT == 0) QT = ctas_qt1 >= 3 * sms ? 2 : 1;
+    if (BN == 0) BN = QT == 2 ? 128 : 96;
   } else if (DP <= 128) {
     if (QT == 0) QT = 1;
     if (BN == 0) BN = (QT == 1 && ctas_qt1 >= 2 * sms) ? 64 : 128;

@@ -169,7 +169,7 @@ def test_head_major_and_strided(cuda_device):
     assert bool((out_buf[:, :, H * D:] == 5.0).all()), "kernel wrote outside the output view"
 
 
-@pytest.mark.parametrize("variant", [0, 1064, 1096, 2064, 2096, 2128])
+@pytest.mark.parametrize("variant", [0, 1064, 1096, 2064, 2096, 2128, 4064])
 def test_running_max_moves(cuda_device, variant):
     """Later key tiles with much larger scores force the lazy running max to move (the O/l correction path)."""
     B, H, Sq, Skv, D = 1, 2, 256, 1024, 40
@@ -189,7 +189,7 @@ def test_custom_scale(cuda_device):
     _check(_run(q, k, v, H, scale=0.05), attention_ref(q, k, v, H, scale=0.05))
 
 
-@pytest.mark.parametrize("variant", [1064, 2064, 2128])
+@pytest.mark.parametrize("variant", [1064, 2064, 2128, 4064])
 def test_forced_timeout_reports_status_and_recovers(cuda_device, variant):
     from npu_ai_b200 import kernels
     dev = torch.device("cuda", 0)
