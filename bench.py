@@ -68,7 +68,7 @@ EX2_PER_CLK_PER_SM = 16  # MUFU exponentials per clock per SM (measured with a p
 
 # DRAM traffic per launch of the dominant kernel (GEMM, mean over the 66 sweep launches of one step) from the ncu
 # capture summarised in profiles/gemm_sweep_dram.md; null when that capture predates the current GEMM kernel.
-GEMM_DRAM_BYTES_PER_LAUNCH = 14401380
+GEMM_DRAM_BYTES_PER_LAUNCH = 14441336
 
 
 def _peaks() -> dict:
