@@ -971,17 +971,22 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   if (QT_req == 4 && (DP > 64 || (BN != 0 && BN != 64)))
     return fail(kErrUnsupported, "four Q tiles per CTA need head dim <= 64 and 64-key tiles (variant %d)", p.variant);
   // Automatic choice (measured on the SD1.5 blocks at batch 2 and 16):
-  //   d <= 64       with at least 3 x SMs one-tile CTAs' worth of query tiles: two Q tiles per CTA with 128-key
-  //                 tiles (three S buffers in the ring): (2, 8, 4096, 4096, 40) 88 us against 94 with 96-key tiles
-  //                 and 96 with four Q tiles; batch 16 592 against 639 / 642 us; (2, 8, 16384, 16384, 40) 1106
-  //                 against 1186 / 1401 us. One Q tile with 96-key tiles for smaller grids.
+  //   d <= 64       two Q tiles per CTA with 128-key tiles (three S buffers in the ring) once their grid reaches
+  //                 2/3 of the SMs, or 1/3 with at least 2048 keys; else one Q tile with 96-key tiles. Measured at
+  //                 d = 40: (2, 8, 4096, 4096) 88 us against 111 with one Q tile, 94 with two of 96-key tiles and 96
+  //                 with four; 8 pairs of 4096 (128 two-tile CTAs) 44 against 66 us; 1 pair of 16384 (64) 157
+  //                 against 171; 4 pairs of 4096 (64) 43 against 47; 16 pairs of 1024 (64, short keys) 14.2
+  //                 against 12.8 with one Q tile; 2 pairs of 4096 (32) 42 against 36.
   //   64 < d <= 128 one Q tile; 64-key tiles (two CTAs per SM) when the grid fills two per SM, else 128.
   //   d > 128       64-key tiles; two Q tiles per CTA when one-tile CTAs would take more than one wave.
   const int64_t ctas_qt1 = (p.Sq + kAttnBM - 1) / kAttnBM * pairs;
   const int64_t sms = dev->sms;
   int QT = QT_req;
   if (DP <= 64) {
-    if (QT == 0) QT = ctas_qt1 >= 3 * sms ? 2 : 1;
+    if (QT == 0) {
+      const int64_t ctas_qt2 = (p.Sq + 2 * kAttnBM - 1) / (2 * kAttnBM) * pairs;
+      QT = (3 * ctas_qt2 >= 2 * sms || (3 * ctas_qt2 >= sms && p.Skv >= 2048)) ? 2 : 1;
+    }
     if (BN == 0) BN = QT == 2 ? 128 : 96;
   } else if (DP <= 128) {
     if (QT == 0) QT = 1;
