@@ -977,6 +977,9 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   //                 with four; 8 pairs of 4096 (128 two-tile CTAs) 44 against 66 us; 1 pair of 16384 (64) 157
   //                 against 171; 4 pairs of 4096 (64) 43 against 47; 16 pairs of 1024 (64, short keys) 14.2
   //                 against 12.8 with one Q tile; 2 pairs of 4096 (32) 42 against 36.
+  //                 Up to 256 keys (one to four 64-key steps, so no S runs ahead and fill and drain dominate): four Q
+  //                 tiles per CTA when their grid reaches half the SMs, else one. The cross-attention (2, 8, 4096, 77)
+  //                 9.4 us against 12.5 with two Q tiles and 10.7 with one; batch 16 60.5 against 82.9 and 61.7.
   //   64 < d <= 128 one Q tile; 64-key tiles (two CTAs per SM) when the grid fills two per SM, else 128.
   //   d > 128       64-key tiles; two Q tiles per CTA when one-tile CTAs would take more than one wave.
   const int64_t ctas_qt1 = (p.Sq + kAttnBM - 1) / kAttnBM * pairs;
@@ -984,8 +987,13 @@ int attention_launch(const AttnProblem& p, cudaStream_t stream) {
   int QT = QT_req;
   if (DP <= 64) {
     if (QT == 0) {
-      const int64_t ctas_qt2 = (p.Sq + 2 * kAttnBM - 1) / (2 * kAttnBM) * pairs;
-      QT = (3 * ctas_qt2 >= 2 * sms || (3 * ctas_qt2 >= sms && p.Skv >= 2048)) ? 2 : 1;
+      if (p.Skv <= 256) {
+        const int64_t ctas_qt4 = (p.Sq + 4 * kAttnBM - 1) / (4 * kAttnBM) * pairs;
+        QT = 2 * ctas_qt4 >= sms ? 4 : 1;
+      } else {
+        const int64_t ctas_qt2 = (p.Sq + 2 * kAttnBM - 1) / (2 * kAttnBM) * pairs;
+        QT = (3 * ctas_qt2 >= 2 * sms || (3 * ctas_qt2 >= sms && p.Skv >= 2048)) ? 2 : 1;
+      }
     }
     if (BN == 0) BN = QT == 2 ? 128 : 96;
   } else if (DP <= 128) {
