@@ -276,19 +276,26 @@ class GpuWorkload:
             h = kernels.register_weight(w)
             self.gemms.append((x, w, b, out, h, 2.0 * M * K * N, 2 * (M * K + N * K + N + M * N)))
         self.attn = []
+        # The attention outputs are views of one flat buffer, so with N > 1 ranks one all-gather per step (after the
+        # last block) moves them all: rank r's outputs land at [r * n, (r + 1) * n) of `attn_full`.
+        sizes = [B * Sq * H * D for (B, H, Sq, Skv, D) in ATTN_BLOCKS]
+        self.attn_out = torch.empty(sum(sizes), dtype=torch.bfloat16, device=device)
+        self.attn_full = torch.empty(world * sum(sizes), dtype=torch.bfloat16, device=device) if world > 1 else None
+        off = 0
         for j, (B, H, Sq, Skv, D) in enumerate(ATTN_BLOCKS):
             s = _attn_seed(rank, j)
             q = _seeded((B, Sq, H * D), 1.0, s, device)
             kk = _seeded((B, Skv, H * D), 1.0, s + 1, device)
             v = _seeded((B, Skv, H * D), 1.0, s + 2, device)
-            out = torch.empty((B, Sq, H * D), dtype=torch.bfloat16, device=device)
-            full = torch.empty((B * world, Sq, H * D), dtype=torch.bfloat16, device=device) if world > 1 else None
-            self.attn.append((q, kk, v, out, full, H, 4.0 * B * H * Sq * Skv * D))
+            out = self.attn_out[off:off + sizes[j]].view(B, Sq, H * D)
+            off += sizes[j]
+            self.attn.append((q, kk, v, out, H, 4.0 * B * H * Sq * Skv * D))
         self.comm = torch.cuda.Stream(device) if world > 1 else None
 
     def step(self, dist, events=None):
-        """One pass: the attention blocks, then the GEMM sweep in M order. With N > 1 ranks each attention output
-        is all-gathered on the communication stream while the sweep runs; the step joins it at the end.
+        """One pass: the attention blocks, then the GEMM sweep in M order. With N > 1 ranks the attention outputs are
+        all-gathered (one NCCL call for all four) on the communication stream while the sweep runs; the step joins
+        it at the end.
 
         `events` (see make_events) marks the start of every attention block, the start of every M group of the
         sweep and the end of the step. Only boundaries carry an event, so launches inside an M group keep their
@@ -296,15 +303,15 @@ class GpuWorkload:
         k = self.k
         main = torch.cuda.current_stream(self.device)
         ei = 0
-        for (q, kk, v, out, full, H, _) in self.attn:
+        for (q, kk, v, out, H, _) in self.attn:
             if events is not None:
                 events[ei].record()
                 ei += 1
             k.attention(q, kk, v, H, out=out)
-            if full is not None:
-                self.comm.wait_stream(main)
-                with torch.cuda.stream(self.comm):
-                    dist.pg.all_gather_into_tensor(full, out)
+        if self.attn_full is not None:
+            self.comm.wait_stream(main)
+            with torch.cuda.stream(self.comm):
+                dist.pg.all_gather_into_tensor(self.attn_full, self.attn_out)
         group = None
         for (x, w, b, out, h, _, _) in self.gemms:
             if events is not None and x.shape[0] != group:
