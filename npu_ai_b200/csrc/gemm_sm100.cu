@@ -267,20 +267,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tma2(&tm_x, stage, dst, kb * kGemmBK, m0);
     }
   };
-  // L2 prefetch of the A box load_x(stage, ., kb, m0) will read.
-  auto prefetch_x = [&](int kb, int m0) {
-    if constexpr (MODE == kModeConv3x3) {
-      const int tap = kb / args.cv_cblocks;
-      const int cb = kb - tap * args.cv_cblocks;
-      const int kh = tap / 3;
-      const int kw = tap - 3 * kh;
-      const int img = m0 / args.cv_hw;
-      const int h0 = (m0 - img * args.cv_hw) / args.cv_w;
-      tma_prefetch_l2_4d(&tm_x, cb * kGemmBK, kw - 1, h0 + kh - 1, img);
-    } else {
-      tma_prefetch_l2_2d(&tm_x, kb * kGemmBK, m0);
-    }
-  };
   // Output columns per tile: BN, or BN/2 gated columns in the GEGLU form (a then gate rows of W in the B tile).
   constexpr int kOutCols = GEGLU ? BN / 2 : BN;
   static_assert(!GEGLU || (BN % 64 == 0), "GEGLU tiles hold two halves of a multiple of 32 columns");
@@ -371,9 +357,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int issued = 0;
       bool ok = true;
       // The weight never depends on the previous kernel on the stream: the first stages' W tiles are requested
-      // before waiting on it (programmatic dependent launch), so their fetch overlaps that kernel's tail. The same
-      // stages' x boxes are prefetched into L2 meanwhile (x may be that kernel's output: an L2 prefetch cannot
-      // return stale data, and when x is already in L2 it costs nothing).
+      // before waiting on it (programmatic dependent launch), so their fetch overlaps that kernel's tail.
       int pre = 0;
       if (unit0 < num_units) {
         int mb, nb;
@@ -384,8 +368,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (rank == 0) mbar_arrive_expect_tx(&full[i], kFullBytes);
           load_w(i, sB + i * L::kBBytes, kb0 + i, nb);
         }
-        const int pm0 = mb * kTileM + int(rank) * kGemmBM;
-        for (int i = 0; i < pre; ++i) prefetch_x(kb0 + i, pm0);
       }
       pdl_wait();  // x may be the previous kernel's output
       for (int unit = unit0; ok && unit < num_units; unit += unit_stride) {

@@ -146,21 +146,6 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
-// Bulk prefetch of one tiled box into L2 (no shared memory, no barrier): warms L2 for a later tma_load of the same
-// box. L2 is the point of coherence of the GPU, so a prefetch issued before the producer of the data has finished
-// never makes the later load read stale data; it only costs bandwidth if the lines are rewritten in between.
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
-               : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int32_t c0, int32_t c1, int32_t c2,
-                                                   int32_t c3) {
-  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(map), "r"(c0),
-               "r"(c1), "r"(c2), "r"(c3)
-               : "memory");
-}
-
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int32_t x,
                                             int32_t y) {
   asm volatile(
